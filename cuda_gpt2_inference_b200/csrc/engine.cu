@@ -1,0 +1,634 @@
+// engine.cu -- whole-model batch-1 decode engine (host C++).
+//
+// Replaces the reference's forward_kv_graph_ready / graph_capture_all /
+// run_generation_once_graph (inference_gpt2_opt.cu:235-596) and its loaders
+// (gpt2_build_from_checkpoint, gpt2_model.h:268-303; gpt2_build_w8,
+// inference_gpt2_opt.cu:143-219).
+//
+// One decode step is 5 kernels per layer + 1 (the reference launches 8-9 per
+// layer + 3):
+//   QKV GEMV   prologue: residual add + LN1 (layer 0: embedding + LN1)
+//   attention  KV append + flash-decoding + merge, one launch
+//   proj GEMV  + bias
+//   FC GEMV    prologue: residual add + LN2; epilogue: bias, GELU, pre-GELU
+//   FCproj     + bias
+//   LM head    prologue: residual add + final LN; epilogue: logits, greedy
+//              pick, next token / position written on the device
+// Kernels are chained with programmatic dependent launch (each stages its
+// weights before waiting on the previous kernel) and several steps are
+// captured into one CUDA graph; because token and position live in device
+// memory and are advanced by the LM head, a graph replays any number of
+// steps with no host round trip.
+//
+// Memory layout in HBM: one parameter arena with the 16 tensors of
+// gpt2_model.h:41-58 in file order (8-bit modes keep the 5 Linear groups as
+// 1-byte codes in their slots, followed by the 5 per-row scale arrays); one
+// activation arena; one KV arena [layer][K|V][head][maxT][hs] (+ scales).
+#include "common.cuh"
+#include "internal.h"
+
+#include <stdio.h>
+#include <string.h>
+#include <string>
+#include <vector>
+
+using namespace gpt2b;
+
+struct gpt2b_engine {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    gpt2b_config cfg{};
+    int wmode = 0, kvmode = 0, wk = 0, kvk = 0;
+    bool w8 = false;
+    size_t xbytes = 2;  // activation element size
+    // arenas
+    unsigned char* params = nullptr;
+    unsigned char* acts = nullptr;
+    unsigned char* kv = nullptr;
+    size_t params_bytes = 0, acts_bytes = 0, kv_bytes = 0;
+    // parameter pointers (file order)
+    unsigned char* p[16] = {};
+    float* sc[5] = {};  // wte, qkvw, attprojw, fcw, fcprojw row scales
+    // activations
+    unsigned char *encoded, *ln1, *qkv, *atty, *res2, *ln2, *fch, *fch_gelu, *res3, *lnf, *proj_out, *fcproj_out;
+    float* logits;
+    float *part_out, *part_max, *part_lse;
+    unsigned* attn_counters;
+    float* lm_val;
+    int* lm_idx;
+    unsigned* lm_counter;
+    int *d_token, *d_pos, *d_history, *d_prompt, *d_nprompt;
+    // kv cache
+    unsigned char* kv_cache = nullptr;
+    float* kv_scale = nullptr;
+    size_t kv_layer_elems = 0, kv_layer_scales = 0;
+    // plans
+    std::vector<GemvParams> qkv_p, proj_p, fc_p, fcproj_p;
+    GemvParams lm_p;
+    int splits = 1;
+    bool use_graph = true, use_pdl = true;
+    int steps_per_graph = 8;
+    cudaGraphExec_t graph_multi = nullptr, graph_one = nullptr;
+    bool graphs_valid = false;
+};
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// Element counts of the 16 parameter tensors (gpt2_model.h:63-87).
+void param_sizes(const gpt2b_config& c, size_t n[16]) {
+    const size_t C = c.channels, L = c.num_layers, Vp = c.padded_vocab_size, maxT = c.max_seq_len;
+    const size_t v[16] = {Vp * C, maxT * C, L * C, L * C, L * 3 * C * C, L * 3 * C, L * C * C, L * C,
+                          L * C, L * C, L * 4 * C * C, L * 4 * C, L * C * 4 * C, L * C, C, C};
+    for (int i = 0; i < 16; i++) n[i] = v[i];
+}
+// tensors stored as 8-bit codes in the mixed file (quantize.cu:190-196)
+const int kLinearSlot[16] = {0, -1, -1, -1, 1, -1, 2, -1, -1, -1, 3, -1, 4, -1, -1, -1};
+
+int check_header(const int* hdr, int wmode, gpt2b_config* cfg) {
+    if (hdr[0] != 20251103) return GPT2B_ERR_FORMAT;
+    const int want = (wmode == GPT2B_W_F32) ? 3 : 5;
+    if (hdr[1] != want) return GPT2B_ERR_FORMAT;
+    cfg->max_seq_len = hdr[2];
+    cfg->vocab_size = hdr[3];
+    cfg->num_layers = hdr[4];
+    cfg->num_heads = hdr[5];
+    cfg->channels = hdr[6];
+    cfg->padded_vocab_size = hdr[7];
+    if (cfg->max_seq_len <= 0 || cfg->vocab_size <= 0 || cfg->num_layers <= 0 || cfg->num_heads <= 0 ||
+        cfg->channels <= 0 || cfg->padded_vocab_size < cfg->vocab_size || cfg->channels % cfg->num_heads != 0)
+        return GPT2B_ERR_FORMAT;
+    return GPT2B_OK;
+}
+
+void free_engine(gpt2b_engine* e) {
+    if (!e) return;
+    DeviceGuard g(e->device);
+    if (e->graph_multi) cudaGraphExecDestroy(e->graph_multi);
+    if (e->graph_one) cudaGraphExecDestroy(e->graph_one);
+    if (e->params) cudaFree(e->params);
+    if (e->acts) cudaFree(e->acts);
+    if (e->kv) cudaFree(e->kv);
+    if (e->stream) cudaStreamDestroy(e->stream);
+    delete e;
+}
+
+// Launches one decode step (5L + 1 kernels) on e->stream.
+cudaError_t launch_step(gpt2b_engine* e) {
+    const int L = e->cfg.num_layers;
+    const bool pdl = e->use_pdl;
+    cudaError_t err;
+    for (int l = 0; l < L; l++) {
+        err = launch_gemv(e->qkv_p[l], e->wk, false, l == 0 ? PRO_EMB_LN : PRO_RES_LN, EPI_STORE, e->stream, pdl);
+        if (err != cudaSuccess) return err;
+        unsigned char* kv_l = e->kv_cache + (size_t)l * e->kv_layer_elems * (e->kvk >= KV_I8 ? 1 : e->xbytes);
+        float* ks_l = e->kv_scale ? e->kv_scale + (size_t)l * e->kv_layer_scales : nullptr;
+        err = launch_attention_engine(e->kvk, e->atty + (size_t)l * e->cfg.channels * e->xbytes, e->qkv, kv_l, ks_l,
+                                      e->d_pos, e->cfg.num_heads, e->cfg.max_seq_len, e->splits, e->part_out,
+                                      e->part_max, e->part_lse, e->attn_counters, e->stream, pdl);
+        if (err != cudaSuccess) return err;
+        err = launch_gemv(e->proj_p[l], e->wk, false, PRO_PLAIN, EPI_STORE, e->stream, pdl);
+        if (err != cudaSuccess) return err;
+        err = launch_gemv(e->fc_p[l], e->wk, false, PRO_RES_LN, EPI_STORE, e->stream, pdl);
+        if (err != cudaSuccess) return err;
+        err = launch_gemv(e->fcproj_p[l], e->wk, false, PRO_PLAIN, EPI_STORE, e->stream, pdl);
+        if (err != cudaSuccess) return err;
+    }
+    return launch_gemv(e->lm_p, e->wk, true, PRO_RES_LN, EPI_LMHEAD, e->stream, pdl);
+}
+
+cudaError_t capture(gpt2b_engine* e, int steps, cudaGraphExec_t* out) {
+    cudaGraph_t g;
+    cudaError_t err = cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal);
+    if (err != cudaSuccess) return err;
+    for (int s = 0; s < steps && err == cudaSuccess; s++) err = launch_step(e);
+    cudaError_t end = cudaStreamEndCapture(e->stream, &g);
+    if (err != cudaSuccess) { if (end == cudaSuccess) cudaGraphDestroy(g); return err; }
+    if (end != cudaSuccess) return end;
+    err = cudaGraphInstantiate(out, g, 0);
+    cudaGraphDestroy(g);
+    return err;
+}
+
+cudaError_t ensure_graphs(gpt2b_engine* e) {
+    if (e->graphs_valid) return cudaSuccess;
+    if (e->graph_multi) { cudaGraphExecDestroy(e->graph_multi); e->graph_multi = nullptr; }
+    if (e->graph_one) { cudaGraphExecDestroy(e->graph_one); e->graph_one = nullptr; }
+    cudaError_t err = capture(e, 1, &e->graph_one);
+    if (err == cudaSuccess && e->steps_per_graph > 1) err = capture(e, e->steps_per_graph, &e->graph_multi);
+    if (err == cudaSuccess) e->graphs_valid = true;
+    return err;
+}
+
+// n forwards from the device-resident token/position.
+cudaError_t run_steps(gpt2b_engine* e, int n) {
+    if (!e->use_graph) {
+        for (int i = 0; i < n; i++) {
+            cudaError_t err = launch_step(e);
+            if (err != cudaSuccess) return err;
+        }
+        return cudaSuccess;
+    }
+    cudaError_t err = ensure_graphs(e);
+    if (err != cudaSuccess) return err;
+    int left = n;
+    if (e->graph_multi)
+        for (; left >= e->steps_per_graph; left -= e->steps_per_graph) {
+            err = cudaGraphLaunch(e->graph_multi, e->stream);
+            if (err != cudaSuccess) return err;
+        }
+    for (; left > 0; left--) {
+        err = cudaGraphLaunch(e->graph_one, e->stream);
+        if (err != cudaSuccess) return err;
+    }
+    return cudaSuccess;
+}
+
+__global__ void set_history_kernel(int* history, const int* d_token, const int* d_pos) {
+    history[*d_pos] = *d_token;
+}
+
+int build_engine(const unsigned char* image, size_t nbytes, const float* scales, size_t nscales, int wmode,
+                 int kvmode, gpt2b_engine** out) {
+    if (!out) return GPT2B_ERR_INVALID_ARG;
+    *out = nullptr;
+    if (wmode < GPT2B_W_F32 || wmode > GPT2B_W_FP8 || (kvmode != GPT2B_KV_FLOATX && kvmode != GPT2B_KV_8BIT))
+        return GPT2B_ERR_INVALID_ARG;
+    const bool w8 = (wmode == GPT2B_W_INT8 || wmode == GPT2B_W_FP8);
+    if (kvmode == GPT2B_KV_8BIT && !w8) return GPT2B_ERR_UNSUPPORTED;  // Makefile:102-103
+    if (!image || nbytes < 1024) return GPT2B_ERR_FORMAT;
+    int hdr[256];
+    memcpy(hdr, image, sizeof(hdr));
+    gpt2b_config cfg;
+    int rc = check_header(hdr, wmode, &cfg);
+    if (rc) return rc;
+    const int C = cfg.channels, L = cfg.num_layers, NH = cfg.num_heads, maxT = cfg.max_seq_len;
+    const int Vp = cfg.padded_vocab_size, hs = C / NH;
+    if (hs != 64 || C > 2048 || maxT % 16 != 0) return GPT2B_ERR_UNSUPPORTED;
+
+    size_t n[16];
+    param_sizes(cfg, n);
+    const size_t xb = (wmode == GPT2B_W_F32) ? 4 : 2;
+    size_t file_bytes = 1024;
+    for (int i = 0; i < 16; i++) file_bytes += n[i] * ((w8 && kLinearSlot[i] >= 0) ? 1 : xb);
+    if (nbytes != file_bytes) return GPT2B_ERR_FORMAT;
+    const size_t n_scales = (size_t)Vp + (size_t)L * 3 * C + (size_t)L * C + (size_t)L * 4 * C + (size_t)L * C;
+    if (w8 && (!scales || nscales != n_scales)) return GPT2B_ERR_FORMAT;
+
+    gpt2b_engine* e = new gpt2b_engine();
+    cudaGetDevice(&e->device);
+    e->cfg = cfg;
+    e->wmode = wmode;
+    e->kvmode = kvmode;
+    e->w8 = w8;
+    e->xbytes = xb;
+    e->wk = (wmode == GPT2B_W_F32) ? WK_F32 : (wmode == GPT2B_W_BF16 ? WK_BF16 : (wmode == GPT2B_W_INT8 ? WK_I8 : WK_FP8));
+    if (kvmode == GPT2B_KV_8BIT) e->kvk = (wmode == GPT2B_W_FP8) ? KV_FP8 : KV_I8;
+    else e->kvk = (wmode == GPT2B_W_F32) ? KV_F32 : KV_BF16;
+
+    cudaError_t err = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
+    auto fail = [&](cudaError_t x) { free_engine(e); return status_from(x); };
+    if (err != cudaSuccess) return fail(err);
+
+    // ---- parameter arena ----
+    size_t off[16], total = 0;
+    for (int i = 0; i < 16; i++) {
+        off[i] = total;
+        total = align256(total + n[i] * ((w8 && kLinearSlot[i] >= 0) ? 1 : xb));
+    }
+    size_t sc_off[5];
+    const size_t sc_n[5] = {(size_t)Vp, (size_t)L * 3 * C, (size_t)L * C, (size_t)L * 4 * C, (size_t)L * C};
+    if (w8)
+        for (int g = 0; g < 5; g++) { sc_off[g] = total; total = align256(total + sc_n[g] * 4); }
+    e->params_bytes = total;
+    if ((err = cudaMalloc(&e->params, total)) != cudaSuccess) return fail(err);
+    const unsigned char* src = image + 1024;
+    for (int i = 0; i < 16; i++) {
+        const size_t b = n[i] * ((w8 && kLinearSlot[i] >= 0) ? 1 : xb);
+        e->p[i] = e->params + off[i];
+        if ((err = cudaMemcpy(e->p[i], src, b, cudaMemcpyHostToDevice)) != cudaSuccess) return fail(err);
+        src += b;
+    }
+    if (w8) {
+        const float* s = scales;
+        for (int g = 0; g < 5; g++) {
+            e->sc[g] = reinterpret_cast<float*>(e->params + sc_off[g]);
+            if ((err = cudaMemcpy(e->sc[g], s, sc_n[g] * 4, cudaMemcpyHostToDevice)) != cudaSuccess) return fail(err);
+            s += sc_n[g];
+        }
+    }
+
+    // ---- activation arena ----
+    const int nsm = sm_count();
+    const int max_chunk = attn_engine_max_chunk(e->kvk);
+    int splits = std::max((maxT + max_chunk - 1) / max_chunk, nsm / NH);
+    if (splits < 1) splits = 1;
+    // engine chunks are multiples of 16 positions and at most max_chunk
+    while (splits > 1 && ((((maxT + splits - 1) / splits) + 15) & ~15) > max_chunk) splits++;
+    e->splits = splits;
+    const int lm_grid_max = 2 * nsm;
+    struct Slot { unsigned char** ptr; size_t bytes; };
+    unsigned char *logits_b, *po_b, *pm_b, *pl_b, *cnt_b, *lmv_b, *lmi_b, *lmc_b, *tok_b, *pos_b, *hist_b, *pr_b, *np_b;
+    std::vector<Slot> slots = {
+        {&e->encoded, C * xb},        {&e->ln1, (size_t)L * C * xb},   {&e->qkv, 3 * (size_t)C * xb},
+        {&e->atty, (size_t)L * C * xb}, {&e->res2, (size_t)L * C * xb}, {&e->ln2, (size_t)L * C * xb},
+        {&e->fch, (size_t)L * 4 * C * xb}, {&e->fch_gelu, 4 * (size_t)C * xb}, {&e->res3, (size_t)L * C * xb},
+        {&e->lnf, C * xb},            {&e->proj_out, C * xb},          {&e->fcproj_out, C * xb},
+        {&logits_b, (size_t)Vp * 4},  {&po_b, (size_t)NH * splits * hs * 4}, {&pm_b, (size_t)NH * splits * 4},
+        {&pl_b, (size_t)NH * splits * 4}, {&cnt_b, (size_t)NH * 4},   {&lmv_b, (size_t)lm_grid_max * 4},
+        {&lmi_b, (size_t)lm_grid_max * 4}, {&lmc_b, 16},               {&tok_b, 16},
+        {&pos_b, 16},                 {&hist_b, (size_t)(maxT + 1) * 4}, {&pr_b, (size_t)maxT * 4},
+        {&np_b, 16}};
+    size_t at = 0;
+    for (auto& s : slots) at = align256(at + s.bytes);
+    e->acts_bytes = at;
+    if ((err = cudaMalloc(&e->acts, at)) != cudaSuccess) return fail(err);
+    if ((err = cudaMemset(e->acts, 0, at)) != cudaSuccess) return fail(err);
+    at = 0;
+    for (auto& s : slots) { *s.ptr = e->acts + at; at = align256(at + s.bytes); }
+    e->logits = reinterpret_cast<float*>(logits_b);
+    e->part_out = reinterpret_cast<float*>(po_b);
+    e->part_max = reinterpret_cast<float*>(pm_b);
+    e->part_lse = reinterpret_cast<float*>(pl_b);
+    e->attn_counters = reinterpret_cast<unsigned*>(cnt_b);
+    e->lm_val = reinterpret_cast<float*>(lmv_b);
+    e->lm_idx = reinterpret_cast<int*>(lmi_b);
+    e->lm_counter = reinterpret_cast<unsigned*>(lmc_b);
+    e->d_token = reinterpret_cast<int*>(tok_b);
+    e->d_pos = reinterpret_cast<int*>(pos_b);
+    e->d_history = reinterpret_cast<int*>(hist_b);
+    e->d_prompt = reinterpret_cast<int*>(pr_b);
+    e->d_nprompt = reinterpret_cast<int*>(np_b);
+
+    // ---- KV arena ----
+    e->kv_layer_elems = 2 * (size_t)NH * maxT * hs;
+    e->kv_layer_scales = (e->kvk >= KV_I8) ? 2 * (size_t)NH * maxT : 0;
+    const size_t kv_elem_b = (e->kvk >= KV_I8) ? 1 : xb;
+    size_t kvb = align256((size_t)L * e->kv_layer_elems * kv_elem_b);
+    const size_t sc_at = kvb;
+    kvb += align256((size_t)L * e->kv_layer_scales * 4);
+    e->kv_bytes = kvb;
+    if ((err = cudaMalloc(&e->kv, kvb)) != cudaSuccess) return fail(err);
+    if ((err = cudaMemset(e->kv, 0, kvb)) != cudaSuccess) return fail(err);
+    e->kv_cache = e->kv;
+    e->kv_scale = e->kv_layer_scales ? reinterpret_cast<float*>(e->kv + sc_at) : nullptr;
+
+    // ---- GEMV plans ----
+    const int wk = e->wk;
+    const size_t wb = (size_t)wkind_bytes(wk);
+    e->qkv_p.resize(L);
+    e->proj_p.resize(L);
+    e->fc_p.resize(L);
+    e->fcproj_p.resize(L);
+    for (int l = 0; l < L; l++) {
+        GemvParams q;
+        q.W = e->p[4] + (size_t)l * 3 * C * C * wb;
+        q.scale = w8 ? e->sc[1] + (size_t)l * 3 * C : nullptr;
+        q.bias = e->p[5] + (size_t)l * 3 * C * xb;
+        q.out = e->qkv;
+        q.M = 3 * C; q.K = C;
+        q.ln_w = e->p[2] + (size_t)l * C * xb;
+        q.ln_b = e->p[3] + (size_t)l * C * xb;
+        q.ln_out = e->ln1 + (size_t)l * C * xb;
+        if (l == 0) {
+            q.d_token = e->d_token; q.d_pos = e->d_pos;
+            q.wte = w8 ? nullptr : e->p[0];
+            q.wte8 = w8 ? e->p[0] : nullptr;
+            q.wte_scale = w8 ? e->sc[0] : nullptr;
+            q.wpe = e->p[1];
+            q.vocab = cfg.vocab_size; q.maxT = maxT;
+            q.res_out = e->encoded;
+        } else {
+            q.res_in = e->res2 + (size_t)(l - 1) * C * xb;
+            q.delta = e->fcproj_out;
+            q.res_out = e->res3 + (size_t)(l - 1) * C * xb;
+        }
+        plan_gemv(q, wk, nsm, true);
+        e->qkv_p[l] = q;
+
+        GemvParams pr;
+        pr.W = e->p[6] + (size_t)l * C * C * wb;
+        pr.scale = w8 ? e->sc[2] + (size_t)l * C : nullptr;
+        pr.bias = e->p[7] + (size_t)l * C * xb;
+        pr.x = e->atty + (size_t)l * C * xb;
+        pr.out = e->proj_out;
+        pr.M = C; pr.K = C;
+        plan_gemv(pr, wk, nsm, true);
+        e->proj_p[l] = pr;
+
+        GemvParams f;
+        f.W = e->p[10] + (size_t)l * 4 * C * C * wb;
+        f.scale = w8 ? e->sc[3] + (size_t)l * 4 * C : nullptr;
+        f.bias = e->p[11] + (size_t)l * 4 * C * xb;
+        f.out = e->fch_gelu;
+        f.pre_gelu = e->fch + (size_t)l * 4 * C * xb;
+        f.do_gelu = 1;
+        f.M = 4 * C; f.K = C;
+        f.res_in = (l == 0) ? e->encoded : e->res3 + (size_t)(l - 1) * C * xb;
+        f.delta = e->proj_out;
+        f.res_out = e->res2 + (size_t)l * C * xb;
+        f.ln_out = e->ln2 + (size_t)l * C * xb;
+        f.ln_w = e->p[8] + (size_t)l * C * xb;
+        f.ln_b = e->p[9] + (size_t)l * C * xb;
+        plan_gemv(f, wk, nsm, true);
+        e->fc_p[l] = f;
+
+        GemvParams fp;
+        fp.W = e->p[12] + (size_t)l * C * 4 * C * wb;
+        fp.scale = w8 ? e->sc[4] + (size_t)l * C : nullptr;
+        fp.bias = e->p[13] + (size_t)l * C * xb;
+        fp.x = e->fch_gelu;
+        fp.out = e->fcproj_out;
+        fp.M = C; fp.K = 4 * C;
+        plan_gemv(fp, wk, nsm, true);
+        e->fcproj_p[l] = fp;
+    }
+    GemvParams lm;
+    lm.W = e->p[0];
+    lm.scale = w8 ? e->sc[0] : nullptr;
+    lm.out = e->logits;
+    lm.M = Vp; lm.K = C;
+    lm.res_in = e->res2 + (size_t)(L - 1) * C * xb;
+    lm.delta = e->fcproj_out;
+    lm.res_out = e->res3 + (size_t)(L - 1) * C * xb;
+    lm.ln_out = e->lnf;
+    lm.ln_w = e->p[14];
+    lm.ln_b = e->p[15];
+    lm.vocab = cfg.vocab_size;
+    lm.part_val = e->lm_val; lm.part_idx = e->lm_idx; lm.counter = e->lm_counter;
+    lm.token_io = e->d_token; lm.pos_io = e->d_pos; lm.history = e->d_history;
+    lm.prompt = e->d_prompt;
+    lm.n_prompt = 0;
+    plan_gemv(lm, wk, nsm, false);
+    if (lm.grid > lm_grid_max) return fail(cudaErrorInvalidConfiguration);
+    e->lm_p = lm;
+    *out = e;
+    return GPT2B_OK;
+}
+
+bool read_file(const char* path, std::vector<unsigned char>& buf) {
+    FILE* f = fopen(path, "rb");
+    if (!f) return false;
+    fseek(f, 0, SEEK_END);
+    long sz = ftell(f);
+    fseek(f, 0, SEEK_SET);
+    if (sz < 0) { fclose(f); return false; }
+    buf.resize((size_t)sz);
+    size_t got = sz ? fread(buf.data(), 1, (size_t)sz, f) : 0;
+    fclose(f);
+    return got == (size_t)sz;
+}
+
+}  // namespace
+
+// The LM head's prompt length is a kernel parameter captured into the graphs;
+// changing it invalidates them.
+static void set_prompt_len(gpt2b_engine* e, int n_prompt) {
+    if (e->lm_p.n_prompt != n_prompt) {
+        e->lm_p.n_prompt = n_prompt;
+        e->graphs_valid = false;
+    }
+}
+
+extern "C" {
+
+int gpt2b_read_header(const char* path, int* version, gpt2b_config* cfg) {
+    if (!path || !cfg) return GPT2B_ERR_INVALID_ARG;
+    FILE* f = fopen(path, "rb");
+    if (!f) return GPT2B_ERR_FILE;
+    int hdr[256];
+    size_t got = fread(hdr, sizeof(int), 256, f);
+    fclose(f);
+    if (got != 256) return GPT2B_ERR_FORMAT;
+    if (hdr[0] != 20251103 || (hdr[1] != 3 && hdr[1] != 5)) return GPT2B_ERR_FORMAT;
+    if (version) *version = hdr[1];
+    return check_header(hdr, hdr[1] == 3 ? GPT2B_W_F32 : GPT2B_W_BF16, cfg);
+}
+
+int gpt2b_engine_create_from_buffer(const void* image, size_t nbytes, const float* scales, size_t nscales, int wmode,
+                                    int kvmode, gpt2b_engine** out) {
+    return build_engine(static_cast<const unsigned char*>(image), nbytes, scales, nscales, wmode, kvmode, out);
+}
+
+int gpt2b_engine_create_from_file(const char* model_path, const char* scale_path, int wmode, int kvmode,
+                                  gpt2b_engine** out) {
+    if (!model_path || !out) return GPT2B_ERR_INVALID_ARG;
+    std::vector<unsigned char> img;
+    if (!read_file(model_path, img)) return GPT2B_ERR_FILE;
+    std::vector<unsigned char> sc;
+    const bool w8 = (wmode == GPT2B_W_INT8 || wmode == GPT2B_W_FP8);
+    if (w8) {
+        std::string sp;
+        if (scale_path) sp = scale_path;
+        else {  // inference_gpt2_opt.cu:666-668
+            std::string m = model_path;
+            if (m.size() < 4) return GPT2B_ERR_FILE;
+            sp = m.substr(0, m.size() - 4) + "_scales.bin";
+        }
+        if (!read_file(sp.c_str(), sc)) return GPT2B_ERR_FILE;
+        if (sc.size() % 4) return GPT2B_ERR_FORMAT;
+    }
+    return build_engine(img.data(), img.size(), w8 ? reinterpret_cast<const float*>(sc.data()) : nullptr,
+                        sc.size() / 4, wmode, kvmode, out);
+}
+
+int gpt2b_engine_destroy(gpt2b_engine* e) {
+    if (!e) return GPT2B_ERR_INVALID_ARG;
+    {
+        DeviceGuard g(e->device);
+        cudaStreamSynchronize(e->stream);
+    }
+    free_engine(e);
+    return GPT2B_OK;
+}
+
+int gpt2b_engine_config(const gpt2b_engine* e, gpt2b_config* cfg) {
+    if (!e || !cfg) return GPT2B_ERR_INVALID_ARG;
+    *cfg = e->cfg;
+    return GPT2B_OK;
+}
+
+int gpt2b_engine_set_option(gpt2b_engine* e, int option, int value) {
+    if (!e) return GPT2B_ERR_INVALID_ARG;
+    switch (option) {
+        case GPT2B_OPT_USE_GRAPH: e->use_graph = value != 0; break;
+        case GPT2B_OPT_USE_PDL: e->use_pdl = value != 0; e->graphs_valid = false; break;
+        case GPT2B_OPT_SPLITS: {
+            const int maxT = e->cfg.max_seq_len, mc = attn_engine_max_chunk(e->kvk);
+            if (value < 1 || ((((maxT + value - 1) / value) + 15) & ~15) > mc) return GPT2B_ERR_INVALID_ARG;
+            if (value > e->splits) return GPT2B_ERR_INVALID_ARG;  // partial buffers are sized at creation
+            e->splits = value;
+            e->graphs_valid = false;
+            break;
+        }
+        case GPT2B_OPT_STEPS_PER_GRAPH:
+            if (value < 1 || value > 64) return GPT2B_ERR_INVALID_ARG;
+            e->steps_per_graph = value;
+            e->graphs_valid = false;
+            break;
+        default: return GPT2B_ERR_INVALID_ARG;
+    }
+    return GPT2B_OK;
+}
+
+int gpt2b_engine_stream(const gpt2b_engine* e, gpt2b_stream_t* stream) {
+    if (!e || !stream) return GPT2B_ERR_INVALID_ARG;
+    *stream = (gpt2b_stream_t)e->stream;
+    return GPT2B_OK;
+}
+
+int gpt2b_engine_device_buffers(const gpt2b_engine* e, float** logits, int** token, int** pos, int** history) {
+    if (!e) return GPT2B_ERR_INVALID_ARG;
+    if (logits) *logits = e->logits;
+    if (token) *token = e->d_token;
+    if (pos) *pos = e->d_pos;
+    if (history) *history = e->d_history;
+    return GPT2B_OK;
+}
+
+int gpt2b_engine_kernels_per_step(const gpt2b_engine* e, int* n) {
+    if (!e || !n) return GPT2B_ERR_INVALID_ARG;
+    *n = 5 * e->cfg.num_layers + 1;
+    return GPT2B_OK;
+}
+
+int gpt2b_engine_forward(gpt2b_engine* e, int token, int pos) {
+    if (!e) return GPT2B_ERR_INVALID_ARG;
+    if (token < 0 || token >= e->cfg.vocab_size || pos < 0 || pos >= e->cfg.max_seq_len) return GPT2B_ERR_INVALID_ARG;
+    DeviceGuard g(e->device);
+    set_prompt_len(e, 0);
+    const int tp[2] = {token, pos};
+    cudaError_t err = cudaMemcpyAsync(e->d_token, &tp[0], sizeof(int), cudaMemcpyHostToDevice, e->stream);
+    if (err == cudaSuccess) err = cudaMemcpyAsync(e->d_pos, &tp[1], sizeof(int), cudaMemcpyHostToDevice, e->stream);
+    if (err == cudaSuccess) err = run_steps(e, 1);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
+    return status_from(err);
+}
+
+int gpt2b_engine_decode(gpt2b_engine* e, int n_steps) {
+    if (!e || n_steps < 0) return GPT2B_ERR_INVALID_ARG;
+    DeviceGuard g(e->device);
+    return status_from(run_steps(e, n_steps));
+}
+
+int gpt2b_engine_history(gpt2b_engine* e, int* out_host, int first, int count) {
+    if (!e || !out_host || first < 0 || count < 0 || first + count > e->cfg.max_seq_len + 1)
+        return GPT2B_ERR_INVALID_ARG;
+    DeviceGuard g(e->device);
+    cudaError_t err = cudaStreamSynchronize(e->stream);
+    if (err == cudaSuccess)
+        err = cudaMemcpy(out_host, e->d_history + first, (size_t)count * sizeof(int), cudaMemcpyDeviceToHost);
+    return status_from(err);
+}
+
+int gpt2b_engine_set_position(gpt2b_engine* e, int token, int pos) {
+    if (!e) return GPT2B_ERR_INVALID_ARG;
+    if (token < 0 || token >= e->cfg.vocab_size || pos < 0 || pos >= e->cfg.max_seq_len) return GPT2B_ERR_INVALID_ARG;
+    DeviceGuard g(e->device);
+    const int tp[2] = {token, pos};  // pageable source: the stream is synchronised before returning
+    cudaError_t err = cudaMemcpyAsync(e->d_token, &tp[0], sizeof(int), cudaMemcpyHostToDevice, e->stream);
+    if (err == cudaSuccess) err = cudaMemcpyAsync(e->d_pos, &tp[1], sizeof(int), cudaMemcpyHostToDevice, e->stream);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
+    return status_from(err);
+}
+
+int gpt2b_engine_generate(gpt2b_engine* e, const int* prompt, int n_prompt, int n_gen, int* out_tokens,
+                          float* logits_host, int sample, unsigned long long seed) {
+    if (!e || !prompt || !out_tokens || n_prompt < 1 || n_gen < 0) return GPT2B_ERR_INVALID_ARG;
+    const int maxT = e->cfg.max_seq_len, V = e->cfg.vocab_size, Vp = e->cfg.padded_vocab_size;
+    if (n_prompt + n_gen > maxT) return GPT2B_ERR_INVALID_ARG;
+    for (int i = 0; i < n_prompt; i++)
+        if (prompt[i] < 0 || prompt[i] >= V) return GPT2B_ERR_INVALID_ARG;
+    DeviceGuard g(e->device);
+    set_prompt_len(e, n_prompt);
+    cudaStream_t st = e->stream;
+    const int zero = 0;
+    cudaError_t err = cudaMemcpyAsync(e->d_prompt, prompt, (size_t)n_prompt * sizeof(int), cudaMemcpyHostToDevice, st);
+    if (err == cudaSuccess) err = cudaMemcpyAsync(e->d_token, prompt, sizeof(int), cudaMemcpyHostToDevice, st);
+    if (err == cudaSuccess) err = cudaMemcpyAsync(e->d_pos, &zero, sizeof(int), cudaMemcpyHostToDevice, st);
+    if (err == cudaSuccess) err = cudaMemcpyAsync(e->d_history, prompt, sizeof(int), cudaMemcpyHostToDevice, st);
+    const int total = n_prompt + n_gen;
+    if (err == cudaSuccess) {
+        if (!logits_host && !sample) {
+            err = run_steps(e, total);  // device-resident: no host round trip per token
+        } else {
+            for (int s = 0; s < total && err == cudaSuccess; s++) {
+                err = run_steps(e, 1);
+                if (err == cudaSuccess && sample && s + 1 >= n_prompt) {
+                    // replace the greedy pick by a softmax sample (step = position of the new token)
+                    int rc = gpt2b_gpu_sample_softmax(e->d_token, e->logits, 1, V, seed, s + 1, (gpt2b_stream_t)st);
+                    if (rc) return rc;
+                    set_history_kernel<<<1, 1, 0, st>>>(e->d_history, e->d_token, e->d_pos);
+                    err = cudaGetLastError();
+                }
+                if (err == cudaSuccess && logits_host)
+                    err = cudaMemcpyAsync(logits_host + (size_t)s * Vp, e->logits, (size_t)Vp * 4,
+                                          cudaMemcpyDeviceToHost, st);
+            }
+        }
+    }
+    if (err == cudaSuccess)
+        err = cudaMemcpyAsync(out_tokens, e->d_history + n_prompt, (size_t)(n_gen + 1) * sizeof(int),
+                              cudaMemcpyDeviceToHost, st);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(st);
+    if (err != cudaSuccess) return status_from(err);
+    int dev = 0;
+    gpt2b_device_error(&dev);
+    return dev ? GPT2B_ERR_DEVICE : GPT2B_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,86 @@
+// internal.h -- host-side interfaces between the library's translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gpt2b {
+
+enum WKind { WK_F32 = 0, WK_BF16 = 1, WK_I8 = 2, WK_FP8 = 3 };
+// x-vector source of a GEMV launch
+enum Prologue {
+    PRO_PLAIN = 0,   // x read from memory
+    PRO_RES_LN = 1,  // r = res_in + delta (stored), x = LayerNorm(r)
+    PRO_EMB_LN = 2   // e = wte[token] + wpe[pos] (stored), x = LayerNorm(e)
+};
+// output of a GEMV launch
+enum Epilogue {
+    EPI_STORE = 0,   // out = gelu?(W.x*scale + b), optional pre_gelu
+    EPI_LMHEAD = 1   // float logits + greedy pick + device-side token/position advance
+};
+
+inline int wkind_bytes(int wk) { return wk == WK_F32 ? 4 : (wk == WK_BF16 ? 2 : 1); }
+
+struct GemvParams {
+    // the matrix-vector product
+    const void* W = nullptr;      // M x K row-major, storage per WKind
+    const float* scale = nullptr; // per-row scale (8-bit kinds)
+    const void* bias = nullptr;   // M, activation type; may be null
+    const void* x = nullptr;      // K, activation type (PRO_PLAIN)
+    void* out = nullptr;          // M, output type
+    void* pre_gelu = nullptr;     // M, output type; may be null
+    int M = 0, K = 0, do_gelu = 0;
+    // tiling (filled by plan_gemv)
+    int rows_per_tile = 0, ntiles = 0, nstages = 1, tile_bytes = 0, grid = 0;
+    // PRO_RES_LN / PRO_EMB_LN
+    const void* res_in = nullptr;  // C, activation type
+    const void* delta = nullptr;   // C, activation type
+    void* res_out = nullptr;       // C, written by block 0
+    void* ln_out = nullptr;        // C, written by block 0 (may be null)
+    const void* ln_w = nullptr;
+    const void* ln_b = nullptr;
+    const int* d_token = nullptr;
+    const int* d_pos = nullptr;
+    const void* wte = nullptr;          // Vp x C activation type (F32/BF16 kinds)
+    const uint8_t* wte8 = nullptr;      // Vp x C codes (8-bit kinds)
+    const float* wte_scale = nullptr;   // Vp
+    const void* wpe = nullptr;          // maxT x C
+    int vocab = 0, maxT = 0;
+    // EPI_LMHEAD
+    float* part_val = nullptr;    // >= grid
+    int* part_idx = nullptr;      // >= grid
+    unsigned* counter = nullptr;  // zero between launches (the last block resets it)
+    int* token_io = nullptr;
+    int* pos_io = nullptr;
+    int* history = nullptr;       // maxT + 1 ints
+    const int* prompt = nullptr;  // device prompt, n_prompt ints
+    int n_prompt = 0;
+    int advance = 1;              // 1: write next token and pos+1; 0: only the logits
+};
+
+// KV-cache storage kinds
+enum KvKind { KV_F32 = 0, KV_BF16 = 1, KV_I8 = 2, KV_FP8 = 3 };
+
+// Decode attention for the engine: fused KV append + flash-decoding over
+// `splits` CTAs per head + last-CTA merge into atty.  kv_layer / kv_scale_layer
+// point at one layer's [K|V] cache and scales; counters (NH) must start at 0.
+cudaError_t launch_attention_engine(int kv, void* atty, const void* qkv, void* kv_layer, float* kv_scale_layer,
+                                    const int* d_pos, int NH, int maxT, int splits, float* part_out,
+                                    float* part_max, float* part_lse, unsigned* counters, cudaStream_t st,
+                                    bool pdl);
+int attn_engine_max_chunk(int kv);  // positions one engine CTA stages at once
+
+// per-translation-unit device error readers
+int gemv_device_error();
+int attention_device_error();
+int norm_device_error();
+int sampler_device_error();
+
+// Chooses rows per tile / stages / grid for an M x K matrix of kind wk.
+// Returns false when the shape cannot be tiled (row larger than a tile).
+bool plan_gemv(GemvParams& p, int wk, int nsm, bool single_wave);
+size_t gemv_smem_bytes(const GemvParams& p, int wk);
+// Dispatches to the kernel instance for (wk, output float?, prologue, epilogue).
+cudaError_t launch_gemv(const GemvParams& p, int wk, bool out_f32, int pro, int epi, cudaStream_t s, bool pdl);
+
+}  // namespace gpt2b

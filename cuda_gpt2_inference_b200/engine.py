@@ -1,0 +1,118 @@
+"""Python handle on the C++ decode engine (``gpt2b_engine_*`` in the C ABI).
+
+Mirrors the reference program's flow (inference_gpt2_opt.cu main, :599-769):
+build the model from a flat-bin image (``gpt2_build_from_checkpoint`` /
+``gpt2_build_w8``), then generate -- with the reference's per-token host round
+trip replaced by device-resident decoding.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import KV_8BIT, KV_FLOATX, W_BF16, W_F32, W_FP8, W_INT8, check, lib
+
+WMODES = {"f32": W_F32, "bf16": W_BF16, "int8": W_INT8, "fp8": W_FP8}
+KVMODES = {"floatx": KV_FLOATX, "8bit": KV_8BIT}
+
+
+class _Config(ctypes.Structure):
+    _fields_ = [("max_seq_len", ctypes.c_int), ("vocab_size", ctypes.c_int), ("padded_vocab_size", ctypes.c_int),
+                ("num_layers", ctypes.c_int), ("num_heads", ctypes.c_int), ("channels", ctypes.c_int)]
+
+
+class Engine:
+    """One decode engine on the current CUDA device."""
+
+    def __init__(self, handle: ctypes.c_void_p):
+        self._h = handle
+        c = _Config()
+        check(lib().gpt2b_engine_config(self._h, ctypes.byref(c)), "gpt2b_engine_config")
+        self.config = dict(maxT=c.max_seq_len, V=c.vocab_size, Vp=c.padded_vocab_size, L=c.num_layers,
+                           NH=c.num_heads, C=c.channels)
+
+    # -- construction ------------------------------------------------------
+    @classmethod
+    def from_buffer(cls, image: bytes, wmode: str = "bf16", kvmode: str = "floatx",
+                    scales: np.ndarray | None = None) -> "Engine":
+        h = ctypes.c_void_p()
+        img = ctypes.create_string_buffer(image, len(image))
+        sc_ptr, nsc = None, 0
+        if scales is not None:
+            scales = np.ascontiguousarray(scales, dtype=np.float32)
+            sc_ptr, nsc = scales.ctypes.data_as(ctypes.c_void_p), scales.size
+        check(lib().gpt2b_engine_create_from_buffer(img, len(image), sc_ptr, nsc, WMODES[wmode], KVMODES[kvmode],
+                                                    ctypes.byref(h)), "gpt2b_engine_create_from_buffer")
+        return cls(h)
+
+    @classmethod
+    def from_file(cls, path: str, wmode: str = "bf16", kvmode: str = "floatx", scale_path: str | None = None):
+        h = ctypes.c_void_p()
+        check(lib().gpt2b_engine_create_from_file(path.encode(), scale_path.encode() if scale_path else None,
+                                                  WMODES[wmode], KVMODES[kvmode], ctypes.byref(h)),
+              "gpt2b_engine_create_from_file")
+        return cls(h)
+
+    def close(self) -> None:
+        if self._h:
+            check(lib().gpt2b_engine_destroy(self._h), "gpt2b_engine_destroy")
+            self._h = None
+
+    def __del__(self):  # best effort
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -- options / buffers ---------------------------------------------------
+    def set_option(self, option: int, value: int) -> None:
+        check(lib().gpt2b_engine_set_option(self._h, option, value), "gpt2b_engine_set_option")
+
+    @property
+    def stream(self) -> int:
+        s = ctypes.c_void_p()
+        check(lib().gpt2b_engine_stream(self._h, ctypes.byref(s)))
+        return s.value or 0
+
+    def device_buffers(self) -> dict:
+        lg, tk, ps, hi = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
+        check(lib().gpt2b_engine_device_buffers(self._h, ctypes.byref(lg), ctypes.byref(tk), ctypes.byref(ps),
+                                                ctypes.byref(hi)))
+        return dict(logits=lg.value, token=tk.value, pos=ps.value, history=hi.value)
+
+    def kernels_per_step(self) -> int:
+        n = ctypes.c_int()
+        check(lib().gpt2b_engine_kernels_per_step(self._h, ctypes.byref(n)))
+        return n.value
+
+    # -- running -------------------------------------------------------------
+    def forward(self, token: int, pos: int) -> None:
+        check(lib().gpt2b_engine_forward(self._h, int(token), int(pos)), "gpt2b_engine_forward")
+
+    def generate(self, prompt, n_gen: int, want_logits: bool = False, sample: bool = False,
+                 seed: int = 1337):
+        """Greedy (or sampled) generation through the C ABI with host buffers.
+        Returns (tokens[n_gen+1], logits[(n_prompt+n_gen), Vp] or None)."""
+        prompt = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(n_gen + 1, np.int32)
+        logits = np.zeros((len(prompt) + n_gen, self.config["Vp"]), np.float32) if want_logits else None
+        check(lib().gpt2b_engine_generate(self._h, prompt.ctypes.data_as(ctypes.c_void_p), len(prompt), n_gen,
+                                          out.ctypes.data_as(ctypes.c_void_p),
+                                          logits.ctypes.data_as(ctypes.c_void_p) if want_logits else None,
+                                          1 if sample else 0, seed), "gpt2b_engine_generate")
+        return out, logits
+
+    def set_position(self, token: int, pos: int) -> None:
+        check(lib().gpt2b_engine_set_position(self._h, int(token), int(pos)), "gpt2b_engine_set_position")
+
+    def history(self, first: int, count: int) -> np.ndarray:
+        """Tokens at positions first..first+count-1 of the device history."""
+        out = np.zeros(count, np.int32)
+        check(lib().gpt2b_engine_history(self._h, out.ctypes.data_as(ctypes.c_void_p), first, count),
+              "gpt2b_engine_history")
+        return out
+
+    def decode(self, n_steps: int) -> None:
+        """Asynchronous device-resident greedy decode on the engine stream."""
+        check(lib().gpt2b_engine_decode(self._h, int(n_steps)), "gpt2b_engine_decode")

@@ -1,0 +1,307 @@
+/*
+ * gpt2_b200.h -- C ABI of the B200-native GPT-2 batch-1 decode library.
+ *
+ * This is the drop-in boundary for the decode hot path of the
+ * CUDA_GPT2_Inference reference (inference_gpt2_opt.cu and the
+ * Inference_gpt2/ operator headers).  The reference exposes header-only C++
+ * templates selected by compile-time precision macros; this library exports
+ * one plain C function per (operator, storage type) instead, with the same
+ * argument order and meaning, plus:
+ *   - an explicit `const int* d_pos` (device pointer to the current length)
+ *     where the reference reads its hidden `__device__ int g_cur_len`
+ *     (Inference_gpt2/attention_kvcache.cuh:39, encoder.cuh:71), so every call
+ *     is CUDA-graph safe without cudaMemcpyToSymbol;
+ *   - an explicit stream on every call (the reference defaults some to 0);
+ *   - an int status return (0 = success) where the reference prints and calls
+ *     exit(1) (GEMV.cuh:27-30, GEMV_w8.cuh:169-170, common.h:123-130).
+ * No function allocates device memory except the engine constructors; the
+ * caller owns every pointer it passes in.
+ *
+ * Type suffixes: _f32 (FP32 storage), _bf16 (BF16 storage), _i8 (INT8 weight
+ * or KV codes), _fp8 (FP8 E4M3 codes).  bf16 arguments are passed as
+ * `uint16_t*` (raw bits), FP8/INT8 codes as `uint8_t*`.
+ */
+#ifndef GPT2_B200_H
+#define GPT2_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* gpt2b_stream_t; /* == cudaStream_t */
+
+/* ---- status codes ------------------------------------------------------- */
+enum {
+    GPT2B_OK = 0,
+    GPT2B_ERR_INVALID_ARG = 1001,  /* a size, pointer or option is out of range */
+    GPT2B_ERR_ALIGNMENT = 1002,    /* a pointer or row pitch is not 16-byte aligned */
+    GPT2B_ERR_UNSUPPORTED = 1003,  /* shape/mode combination not implemented */
+    GPT2B_ERR_FILE = 1004,         /* weight/scale file missing or unreadable */
+    GPT2B_ERR_FORMAT = 1005,       /* bad magic/version/header/size in a weight image */
+    GPT2B_ERR_DEVICE = 1006,       /* a kernel reported an error word (see gpt2b_device_error) */
+    GPT2B_ERR_NCCL = 1007,         /* a collective call failed or timed out */
+    GPT2B_ERR_CUDA = 2000          /* GPT2B_ERR_CUDA + cudaError_t */
+};
+/* device error words (gpt2b_device_error) */
+enum {
+    GPT2B_DEVERR_MBAR_TIMEOUT = 1, /* a bulk copy never completed within its bound */
+    GPT2B_DEVERR_BAD_TOKEN = 2,    /* token id outside [0, vocab) */
+    GPT2B_DEVERR_BAD_POS = 3,      /* position outside [0, maxT) */
+    GPT2B_DEVERR_PEER_TIMEOUT = 4  /* a cross-GPU flag wait hit its bound */
+};
+
+const char* gpt2b_status_string(int status);
+/* Reads and clears the device error word of the current device (0 = none). */
+int gpt2b_device_error(int* code);
+int gpt2b_version(void);
+
+/* ======================================================================== */
+/* Decode GEMVs                                                              */
+/* ======================================================================== */
+/* out[m] = sum_k W[m,k] x[k], FP32 output, no bias.
+ * Replaces launch_GEMV6<T> (Inference_gpt2/GEMV.cuh:112; lab twin gemv/GEMV.cu:419).
+ * W row-major M x K; K*sizeof(T) must be a multiple of 16 and W 16-byte aligned.
+ * Also the FP32/BF16 LM head: replaces matmul_forward_cublaslt_f32
+ * (Inference_gpt2/matmul.cuh:158, called at inference_gpt2_opt.cu:399) with
+ * M = Vp, W = wte. */
+int gpt2b_launch_GEMV6_f32(float* out, const float* W, const float* x, int M, int K, gpt2b_stream_t stream);
+int gpt2b_launch_GEMV6_bf16(float* out, const uint16_t* W, const uint16_t* x, int M, int K,
+                            gpt2b_stream_t stream);
+
+/* pre = W.x + bias (bias may be NULL); pre_gelu[m] <- pre when pre_gelu != NULL;
+ * out = do_gelu ? gelu_tanh(pre) : pre, stored in the storage type.
+ * Replaces launch_GEMV6_fused<T,OT,BT> (Inference_gpt2/GEMV.cuh:204) as used by
+ * matmul_forward (inference_gpt2_opt.cu:106-116). */
+int gpt2b_launch_GEMV6_fused_f32(float* out, float* pre_gelu, const float* W, const float* x, const float* bias,
+                                 int M, int K, int do_gelu, gpt2b_stream_t stream);
+int gpt2b_launch_GEMV6_fused_bf16(uint16_t* out, uint16_t* pre_gelu, const uint16_t* W, const uint16_t* x,
+                                  const uint16_t* bias, int M, int K, int do_gelu, gpt2b_stream_t stream);
+
+/* 8-bit weight-only GEMV: pre = scale[m] * sum_k decode(W[m,k]) x[k] + bias[m];
+ * epilogue as above.  x, bias, out, pre_gelu are BF16.  K % 16 == 0.
+ * Replaces launch_GEMV6_w8x2<floatX,floatX> (Inference_gpt2/GEMV_w8.cuh:162)
+ * as used by matmul_forward_w8 (inference_gpt2_opt.cu:121-131). */
+int gpt2b_launch_GEMV6_w8x2_i8(uint16_t* out, uint16_t* pre_gelu, const uint8_t* W, const uint16_t* x,
+                               const float* scale, const uint16_t* bias, int M, int K, int do_gelu,
+                               gpt2b_stream_t stream);
+int gpt2b_launch_GEMV6_w8x2_fp8(uint16_t* out, uint16_t* pre_gelu, const uint8_t* W, const uint16_t* x,
+                                const float* scale, const uint16_t* bias, int M, int K, int do_gelu,
+                                gpt2b_stream_t stream);
+/* FP32-output form used for the 8-bit LM head, bias NULL, M = Vp: replaces
+ * launch_GEMV6_w8x2<float,floatX> (inference_gpt2_opt.cu:394). */
+int gpt2b_launch_GEMV6_w8x2_i8_f32out(float* out, const uint8_t* W, const uint16_t* x, const float* scale,
+                                      int M, int K, gpt2b_stream_t stream);
+int gpt2b_launch_GEMV6_w8x2_fp8_f32out(float* out, const uint8_t* W, const uint16_t* x, const float* scale,
+                                       int M, int K, gpt2b_stream_t stream);
+
+/* out[r,c] = bf16(decode(w8[r,c]) * scale[r]).  Replaces dequant_wte_kernel
+ * (Inference_gpt2/GEMV_w8.cuh:179, launched at inference_gpt2_opt.cu:214). */
+int gpt2b_dequant_wte_i8(const uint8_t* w8, const float* scale, uint16_t* out, int Vp, int C,
+                         gpt2b_stream_t stream);
+int gpt2b_dequant_wte_fp8(const uint8_t* w8, const float* scale, uint16_t* out, int Vp, int C,
+                          gpt2b_stream_t stream);
+
+/* Per-row symmetric quantiser: s = amax/127 (INT8) or amax/448 (FP8), s = 1 for
+ * an all-zero row, codes = encode(W/s).  Bit-exact with quant_rows
+ * (quantize.cu:41-81) built with the reference's --use_fast_math. */
+int gpt2b_quant_rows_i8(const float* W, uint8_t* W8, float* scale, int M, int K, gpt2b_stream_t stream);
+int gpt2b_quant_rows_fp8(const float* W, uint8_t* W8, float* scale, int M, int K, gpt2b_stream_t stream);
+/* Whole-file quantiser: BF16 v5 image in, 8-bit mixed image + float32 per-row
+ * scales out (the 5 Linear groups wte, qkvw, attprojw, fcw, fcprojw as codes,
+ * the other 11 tensors unchanged, header unchanged), byte-compatible with the
+ * quantize tool (quantize.cu:83-233).  fp8 = 0: INT8, 1: FP8 E4M3.  Runs on the
+ * current device.  The buffer form writes into caller memory: out8 must hold
+ * gpt2b_quantized_size() bytes and scales gpt2b_quantized_scale_count() floats. */
+int gpt2b_quantize_file(const char* in_bf16_path, const char* out8_path, const char* scale_path, int fp8);
+int gpt2b_quantized_size(const void* bf16_image, size_t nbytes, size_t* out8_bytes, size_t* scale_count);
+int gpt2b_quantize_buffer(const void* bf16_image, size_t nbytes, void* out8, float* scales, int fp8);
+
+/* ======================================================================== */
+/* KV cache and decode attention                                             */
+/* ======================================================================== */
+/* Layout (attention_kvcache.cuh:8-13): one layer's cache is [K | V], each
+ * B*NH*maxT*hs elements; element (b,h,j,d) at ((b*NH+h)*maxT + j)*hs + d.
+ * 8-bit scales: [K | V], each B*NH*maxT floats, index (b*NH+h)*maxT + j
+ * (attention_kvcache_w8.cuh:129-131).  qkv is [Q(NH*hs) | K | V] per batch row.
+ * hs must be 64 (the reference's thread mapping fixes it); *d_pos < maxT. */
+
+/* Append K,V of the current token at position *d_pos.  Replaces
+ * kv_cache_write_kernel (attention_kvcache.cuh:46) / kv_cache_write_kernel_w8
+ * (attention_kvcache_w8.cuh:115). */
+int gpt2b_kv_cache_write_f32(float* kv_cache, const float* qkv, int B, int NH, int hs, int maxT,
+                             const int* d_pos, gpt2b_stream_t stream);
+int gpt2b_kv_cache_write_bf16(uint16_t* kv_cache, const uint16_t* qkv, int B, int NH, int hs, int maxT,
+                              const int* d_pos, gpt2b_stream_t stream);
+int gpt2b_kv_cache_write_w8_i8(uint8_t* kv_cache, float* kv_scale, const uint16_t* qkv, int B, int NH, int hs,
+                               int maxT, const int* d_pos, gpt2b_stream_t stream);
+int gpt2b_kv_cache_write_w8_fp8(uint8_t* kv_cache, float* kv_scale, const uint16_t* qkv, int B, int NH, int hs,
+                                int maxT, const int* d_pos, gpt2b_stream_t stream);
+
+/* out = softmax(q.K^T / sqrt(hs)) V over positions [0, *d_pos], one pass per
+ * head.  Replaces attention_forward_kv_small (attention_kvcache.cuh:453) and
+ * attention_forward_kv_small_w8 (attention_kvcache_w8.cuh:529). */
+int gpt2b_attention_forward_kv_small_f32(float* out, const float* qkv, const float* kv_cache, int B, int NH,
+                                         int hs, int maxT, const int* d_pos, gpt2b_stream_t stream);
+int gpt2b_attention_forward_kv_small_bf16(uint16_t* out, const uint16_t* qkv, const uint16_t* kv_cache, int B,
+                                          int NH, int hs, int maxT, const int* d_pos, gpt2b_stream_t stream);
+int gpt2b_attention_forward_kv_small_w8_i8(uint16_t* out, const uint16_t* qkv, const uint8_t* kv_cache,
+                                           const float* kv_scale, int B, int NH, int hs, int maxT,
+                                           const int* d_pos, gpt2b_stream_t stream);
+int gpt2b_attention_forward_kv_small_w8_fp8(uint16_t* out, const uint16_t* qkv, const uint8_t* kv_cache,
+                                            const float* kv_scale, int B, int NH, int hs, int maxT,
+                                            const int* d_pos, gpt2b_stream_t stream);
+
+/* Flash-decoding: split [0, *d_pos] into S chunks of ceil((pos+1)/S), write
+ * per-split partials (part_out un-normalised [B*NH*S*hs], part_max, part_lse
+ * [B*NH*S]; an empty split writes max=-FLT_MAX, lse=0, out=0), then merge.
+ * Graph-capturable.  Replaces attention_forward_kv_large(_w8)
+ * (attention_kvcache.cuh:464, attention_kvcache_w8.cuh:541) and the raw
+ * split+merge launches of inference_gpt2_opt.cu:310-314,338-341. */
+int gpt2b_attention_forward_kv_large_f32(float* out, const float* qkv, const float* kv_cache, int B, int NH,
+                                         int hs, int maxT, const int* d_pos, gpt2b_stream_t stream,
+                                         float* part_out, float* part_lse, float* part_max, int S);
+int gpt2b_attention_forward_kv_large_bf16(uint16_t* out, const uint16_t* qkv, const uint16_t* kv_cache, int B,
+                                          int NH, int hs, int maxT, const int* d_pos, gpt2b_stream_t stream,
+                                          float* part_out, float* part_lse, float* part_max, int S);
+int gpt2b_attention_forward_kv_large_w8_i8(uint16_t* out, const uint16_t* qkv, const uint8_t* kv_cache,
+                                           const float* kv_scale, int B, int NH, int hs, int maxT,
+                                           const int* d_pos, gpt2b_stream_t stream, float* part_out,
+                                           float* part_lse, float* part_max, int S);
+int gpt2b_attention_forward_kv_large_w8_fp8(uint16_t* out, const uint16_t* qkv, const uint8_t* kv_cache,
+                                            const float* kv_scale, int B, int NH, int hs, int maxT,
+                                            const int* d_pos, gpt2b_stream_t stream, float* part_out,
+                                            float* part_lse, float* part_max, int S);
+/* The two halves on their own: attention_kv_split_kernel(_w8)
+ * (attention_kvcache.cuh:185, _w8.cuh:260) and attention_kv_merge_kernel(_w8)
+ * (attention_kvcache.cuh:298, _w8.cuh:374). */
+int gpt2b_attention_kv_split_bf16(float* part_out, float* part_lse, float* part_max, const uint16_t* qkv,
+                                  const uint16_t* kv_cache, int B, int NH, int hs, int maxT, int S,
+                                  const int* d_pos, gpt2b_stream_t stream);
+int gpt2b_attention_kv_merge_bf16(uint16_t* out, const float* part_out, const float* part_lse,
+                                  const float* part_max, int B, int NH, int hs, int S, gpt2b_stream_t stream);
+int gpt2b_attention_kv_merge_f32(float* out, const float* part_out, const float* part_lse, const float* part_max,
+                                 int B, int NH, int hs, int S, gpt2b_stream_t stream);
+
+/* ======================================================================== */
+/* LayerNorm, residual, embedding                                            */
+/* ======================================================================== */
+/* out = (x-mean)*rstd*w + b per row of C; mean/rstd (float, may be NULL).
+ * Replaces layernorm_forward (Inference_gpt2/layernorm.cuh:282). N = B*T rows. */
+int gpt2b_layernorm_forward_f32(float* out, float* mean, float* rstd, const float* inp, const float* weight,
+                                const float* bias, int B, int T, int C, gpt2b_stream_t stream);
+int gpt2b_layernorm_forward_bf16(uint16_t* out, float* mean, float* rstd, const uint16_t* inp,
+                                 const uint16_t* weight, const uint16_t* bias, int B, int T, int C,
+                                 gpt2b_stream_t stream);
+/* residual = inp1 + inp2 (stored), normed = LN(residual).  Replaces
+ * fused_residual_forward5 (Inference_gpt2/layernorm.cuh:336). */
+int gpt2b_fused_residual_forward5_f32(float* residual, float* normed, float* mean, float* rstd, const float* inp1,
+                                      const float* inp2, const float* weight, const float* bias, int N, int C,
+                                      gpt2b_stream_t stream);
+int gpt2b_fused_residual_forward5_bf16(uint16_t* residual, uint16_t* normed, float* mean, float* rstd,
+                                       const uint16_t* inp1, const uint16_t* inp2, const uint16_t* weight,
+                                       const uint16_t* bias, int N, int C, gpt2b_stream_t stream);
+/* out[b] = wte[inp[b]] + wpe[*d_pos].  Replaces encoder_forward_kv
+ * (Inference_gpt2/encoder.cuh:87). */
+int gpt2b_encoder_forward_kv_f32(float* out, const int* inp, const float* wte, const float* wpe, const int* d_pos,
+                                 int B, int C, gpt2b_stream_t stream);
+int gpt2b_encoder_forward_kv_bf16(uint16_t* out, const int* inp, const uint16_t* wte, const uint16_t* wpe,
+                                  const int* d_pos, int B, int C, gpt2b_stream_t stream);
+
+/* ======================================================================== */
+/* Token selection                                                           */
+/* ======================================================================== */
+/* Softmax sampling with Philox(seed, subsequence=b, offset=step) uniform draws
+ * (curand), one token per batch row.  Replaces gpu_sample_softmax
+ * (Inference_gpt2/sampler_gpu.cuh:94); same ordering of the cumulative sum. */
+int gpt2b_gpu_sample_softmax(int* d_token, const float* logits, int B, int V, unsigned long long seed, int step,
+                             gpt2b_stream_t stream);
+/* Greedy pick: index of the largest logit among the first V, lowest index on
+ * ties.  No counterpart in the reference (it only samples); the greedy decode
+ * configurations need it. */
+int gpt2b_gpu_argmax(int* d_token, const float* logits, int B, int V, int ld, gpt2b_stream_t stream);
+
+/* ======================================================================== */
+/* Whole-model decode engine (replaces forward_kv_graph_ready,               */
+/* graph_capture_all and run_generation_once_graph, inference_gpt2_opt.cu)   */
+/* ======================================================================== */
+/* Weight storage modes (the reference's PRECISION switch, Makefile:62-85). */
+enum { GPT2B_W_F32 = 0, GPT2B_W_BF16 = 1, GPT2B_W_INT8 = 2, GPT2B_W_FP8 = 3 };
+/* KV-cache modes: the activation type, or 8-bit codes in the weights' format
+ * with one float scale per (K/V, layer, head, position) (Makefile:96-105). */
+enum { GPT2B_KV_FLOATX = 0, GPT2B_KV_8BIT = 1 };
+/* Engine options (gpt2b_engine_set_option). */
+enum {
+    GPT2B_OPT_USE_GRAPH = 1,  /* 1 (default): replay the captured step graph; 0: launch kernels */
+    GPT2B_OPT_USE_PDL = 2,    /* 1 (default): programmatic dependent launch between kernels */
+    GPT2B_OPT_SPLITS = 3,     /* attention splits per head for long contexts (default: fills the SMs) */
+    GPT2B_OPT_STEPS_PER_GRAPH = 4 /* decode steps captured into one graph (default 8) */
+};
+
+/* GPT2Config field order (Inference_gpt2/gpt2_model.h:28-35). */
+typedef struct {
+    int max_seq_len;
+    int vocab_size;
+    int padded_vocab_size;
+    int num_layers;
+    int num_heads;
+    int channels;
+} gpt2b_config;
+
+typedef struct gpt2b_engine gpt2b_engine;
+
+/* Reads the 256-int header of a flat-bin weight file (gpt2_model.h:268-296).
+ * Host only.  version: 3 = FP32, 5 = BF16 or 8-bit mixed. */
+int gpt2b_read_header(const char* path, int* version, gpt2b_config* cfg);
+
+/* Builds an engine on the current device from a weight image in the
+ * reference format: v3 FP32 / v5 BF16 (gpt2_build_from_checkpoint,
+ * gpt2_model.h:268-303) or the 8-bit mixed file of quantize.cu:190-229 with
+ * its per-row scales (gpt2_build_w8, inference_gpt2_opt.cu:143-219).
+ * One device arena holds all parameters; another the activations; the KV
+ * cache is a third.  scale_path may be NULL: then "<model minus .bin>_scales.bin"
+ * is used as in inference_gpt2_opt.cu:666-668. */
+int gpt2b_engine_create_from_file(const char* model_path, const char* scale_path, int wmode, int kvmode,
+                                  gpt2b_engine** out);
+int gpt2b_engine_create_from_buffer(const void* image, size_t nbytes, const float* scales, size_t nscales,
+                                    int wmode, int kvmode, gpt2b_engine** out);
+int gpt2b_engine_destroy(gpt2b_engine* e);
+int gpt2b_engine_config(const gpt2b_engine* e, gpt2b_config* cfg);
+int gpt2b_engine_set_option(gpt2b_engine* e, int option, int value);
+int gpt2b_engine_stream(const gpt2b_engine* e, gpt2b_stream_t* stream);
+/* Device pointers owned by the engine: logits (Vp floats), the current token
+ * and position (int), and the token history (maxT+1 ints). */
+int gpt2b_engine_device_buffers(const gpt2b_engine* e, float** logits, int** token, int** pos, int** history);
+
+/* One forward of `token` at position `pos` on the engine stream (host
+ * values; copied to the engine's device slots).  Logits land in the engine's
+ * logits buffer.  The equivalent of gpt2_forward_kv (inference_gpt2_opt.cu:403). */
+int gpt2b_engine_forward(gpt2b_engine* e, int token, int pos);
+/* Teacher-forced prompt at positions 0..n_prompt-1 then n_gen greedy steps;
+ * out_tokens (host) receives n_gen+1 tokens (the pick after the prompt and
+ * after each step).  logits_host (optional) receives (n_prompt+n_gen) x Vp
+ * floats.  Host buffers; copies included.  sample != 0 uses
+ * gpt2b_gpu_sample_softmax(seed, step) instead of greedy. */
+int gpt2b_engine_generate(gpt2b_engine* e, const int* prompt, int n_prompt, int n_gen, int* out_tokens,
+                          float* logits_host, int sample, unsigned long long seed);
+/* Device-resident decode: starting from the token and position already in the
+ * engine's device slots, run n_steps greedy forwards without host round trips
+ * (token and position advance on the device; picks are appended to the
+ * device history).  Asynchronous on the engine stream. */
+int gpt2b_engine_decode(gpt2b_engine* e, int n_steps);
+/* Sets the device token/position slots (asynchronous copy on the engine
+ * stream) so gpt2b_engine_decode continues from (token, pos); the KV cache
+ * below pos is kept. */
+int gpt2b_engine_set_position(gpt2b_engine* e, int token, int pos);
+/* Waits for the engine stream and copies history[first .. first+count) (the
+ * token at each position; history[p+1] is the pick after position p) to host. */
+int gpt2b_engine_history(gpt2b_engine* e, int* out_host, int first, int count);
+/* Kernel launches one step issues (for launch accounting). */
+int gpt2b_engine_kernels_per_step(const gpt2b_engine* e, int* n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GPT2_B200_H */

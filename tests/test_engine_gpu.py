@@ -1,0 +1,176 @@
+"""Whole-model decode parity on the GPU.
+
+* Small models in every precision mode against the CPU oracle, teacher-forced
+  on the engine's own tokens (so a late divergence in greedy picks cannot hide
+  an early numerical difference), plus FP32 greedy tokens identical.
+* GPT-2 124M FP32: 24-token prompt + 128 greedy steps, tokens identical to the
+  oracle and logits cosine >= 0.9999 at every step.
+* GPT-2 124M BF16 / INT8+KV8 / FP8+KV8 against the reference decode engine
+  compiled from source (oracle/_ref/libref_engine_*.so), teacher-forced.
+* Launch modes (CUDA graph / eager, PDL on/off, device-resident decode) give
+  bit-identical results.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from conftest import cosine
+
+pytestmark = pytest.mark.gpu
+
+MODES = [("f32", "floatx"), ("bf16", "floatx"), ("int8", "floatx"), ("int8", "8bit"), ("fp8", "8bit"),
+         ("fp8", "floatx")]
+
+
+def _quantize(gpt2b, img16: bytes, fmt: str):
+    lib = gpt2b.lib()
+    ob, ns = ctypes.c_size_t(), ctypes.c_size_t()
+    gpt2b.check(lib.gpt2b_quantized_size(img16, len(img16), ctypes.byref(ob), ctypes.byref(ns)))
+    out = ctypes.create_string_buffer(ob.value)
+    sc = np.zeros(ns.value, np.float32)
+    gpt2b.check(lib.gpt2b_quantize_buffer(img16, len(img16), out, sc.ctypes.data_as(ctypes.c_void_p),
+                                          1 if fmt == "fp8" else 0), "quantize")
+    return out.raw, sc
+
+
+def _images(gpt2b, cfg, seed, init):
+    from cuda_gpt2_inference_b200 import weights
+    p = weights.synth_params(cfg, seed, init=init)
+    imgs = {"f32": (weights.image(p, cfg, "f32"), None), "bf16": (weights.image(p, cfg, "bf16"), None)}
+    for fmt in ("int8", "fp8"):
+        imgs[fmt] = _quantize(gpt2b, imgs["bf16"][0], fmt)
+    return imgs
+
+
+@pytest.fixture(scope="module")
+def mini(gpt2b, cuda):
+    from cuda_gpt2_inference_b200 import weights
+    cfg = weights.mini_config(L=2, NH=2, maxT=64, V=500, Vp=512)
+    return cfg, _images(gpt2b, cfg, 31, "test")
+
+
+@pytest.mark.parametrize("wmode,kvmode", MODES)
+def test_mini_model_matches_oracle(mini, orc, wmode, kvmode):
+    from cuda_gpt2_inference_b200.engine import Engine
+    cfg, imgs = mini
+    img, sc = imgs[wmode]
+    eng = Engine.from_buffer(img, wmode, kvmode, sc)
+    prompt = [5, 17, 123, 499, 0]
+    n_gen = cfg["maxT"] - len(prompt)
+    toks, lg = eng.generate(prompt, n_gen, want_logits=True)
+    m = orc.Model(img, wmode, kvmode, sc)
+    seq = list(prompt) + list(toks[:-1])
+    floor = 0.99999 if wmode == "f32" else 0.999
+    worst = 1.0
+    for pos, t in enumerate(seq):
+        ref = m.step(int(t), pos)
+        worst = min(worst, cosine(lg[pos], ref))
+        if wmode == "f32":
+            assert int(np.argmax(ref[: cfg["V"]])) == int(np.argmax(lg[pos][: cfg["V"]])), pos
+    assert worst >= floor, worst
+    if wmode == "f32":
+        m.reset()
+        otoks, _ = m.generate(prompt, n_gen)
+        assert np.array_equal(otoks, toks)
+    eng.close()
+
+
+def test_launch_modes_bit_identical(mini):
+    from cuda_gpt2_inference_b200 import OPT_STEPS_PER_GRAPH, OPT_USE_GRAPH, OPT_USE_PDL
+    from cuda_gpt2_inference_b200.engine import Engine
+    cfg, imgs = mini
+    img, _ = imgs["bf16"]
+    prompt = [1, 2, 3]
+    results = []
+    for graph, pdl, spg in ((1, 1, 8), (0, 1, 8), (1, 0, 8), (0, 0, 1), (1, 1, 3)):
+        eng = Engine.from_buffer(img, "bf16")
+        eng.set_option(OPT_USE_GRAPH, graph)
+        eng.set_option(OPT_USE_PDL, pdl)
+        eng.set_option(OPT_STEPS_PER_GRAPH, spg)
+        toks, lg = eng.generate(prompt, 40, want_logits=True)
+        results.append((toks, lg))
+        fast, _ = eng.generate(prompt, 40)  # device-resident path
+        assert np.array_equal(fast, toks)
+        eng.close()
+    for toks, lg in results[1:]:
+        assert np.array_equal(toks, results[0][0]) and np.array_equal(lg, results[0][1])
+
+
+def test_engine_rejects_bad_inputs(mini, gpt2b):
+    from cuda_gpt2_inference_b200.engine import Engine
+    cfg, imgs = mini
+    eng = Engine.from_buffer(imgs["bf16"][0], "bf16")
+    with pytest.raises(gpt2b.Gpt2bError):
+        eng.forward(cfg["V"], 0)  # token out of range
+    with pytest.raises(gpt2b.Gpt2bError):
+        eng.forward(1, cfg["maxT"])  # position out of range
+    with pytest.raises(gpt2b.Gpt2bError):
+        eng.generate([1, 2], cfg["maxT"])  # prompt + generation longer than the context
+    eng.forward(1, 0)
+    assert gpt2b.device_error() == 0
+    eng.close()
+
+
+# ------------------------------------------------------------- 124M -------
+@pytest.fixture(scope="module")
+def m124(gpt2b, cuda):
+    from cuda_gpt2_inference_b200 import weights
+    return weights.GPT2_124M, _images(gpt2b, weights.GPT2_124M, 1234, "spec")
+
+
+@pytest.mark.slow
+def test_124m_fp32_greedy_128_steps(m124, orc):
+    from cuda_gpt2_inference_b200.engine import Engine
+    cfg, imgs = m124
+    img, _ = imgs["f32"]
+    rng = np.random.default_rng(24)
+    prompt = rng.integers(0, cfg["V"], 24).astype(np.int32)
+    eng = Engine.from_buffer(img, "f32")
+    toks, lg = eng.generate(prompt, 128, want_logits=True)
+    eng.close()
+    m = orc.Model(img, "f32")
+    otoks, olg = m.generate(prompt, 128, want_logits=True)
+    assert np.array_equal(toks, otoks), (toks[:20], otoks[:20])
+    cos = [cosine(lg[i], olg[i]) for i in range(len(lg))]
+    assert min(cos) >= 0.9999, min(cos)
+
+
+def _ref_engine(orc, name, path):
+    if not orc.ref_available(f"libref_engine_{name}.so"):
+        pytest.skip("reference engine not built")
+    lib = orc.ref_gpu(f"engine_{name}")
+    lib.ref_engine_init.argtypes = [ctypes.c_char_p, ctypes.c_int]
+    lib.ref_engine_step.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+    assert lib.ref_engine_init(str(path).encode(), 0 if name in ("f32", "bf16") else 1) == 0
+    return lib
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("wmode,kvmode,refname", [("bf16", "floatx", "bf16"), ("int8", "8bit", "int8kv8"),
+                                                  ("fp8", "8bit", "fp8kv8")])
+def test_124m_against_reference_engine(m124, orc, tmp_path, wmode, kvmode, refname):
+    from cuda_gpt2_inference_b200.engine import Engine
+    cfg, imgs = m124
+    img, sc = imgs[wmode]
+    path = tmp_path / "model.bin"
+    path.write_bytes(img)
+    if sc is not None:
+        (tmp_path / "model_scales.bin").write_bytes(sc.tobytes())
+    ref = _ref_engine(orc, refname, path)
+    rng = np.random.default_rng(5)
+    prompt = rng.integers(0, cfg["V"], 24).astype(np.int32)
+    n_gen = 176  # crosses the reference's 150-position switch to split+merge
+    eng = Engine.from_buffer(img, wmode, kvmode, sc)
+    toks, lg = eng.generate(prompt, n_gen, want_logits=True)
+    eng.close()
+    seq = list(prompt) + list(toks[:-1])
+    row = np.zeros(cfg["Vp"], np.float32)
+    cos = []
+    for pos, t in enumerate(seq):
+        assert ref.ref_engine_step(int(t), pos, row.ctypes.data_as(ctypes.c_void_p)) == 0
+        cos.append(cosine(lg[pos], row))
+    floor = 0.999 if wmode == "bf16" else 0.998
+    assert min(cos) >= floor, (min(cos), int(np.argmin(cos)))
