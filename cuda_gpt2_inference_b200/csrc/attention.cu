@@ -522,8 +522,7 @@ template <typename OT>
 static int attn_merge(OT* out, const float* po, const float* pl, const float* pm, int B, int NH, int hs, int S,
                       cudaStream_t st) {
     if (B <= 0 || NH <= 0 || hs <= 0 || hs > 1024 || S <= 0 || !out) return GPT2B_ERR_INVALID_ARG;
-    attn_merge_kernel<OT><<<B * NH, ((hs + 31) / 32) * 32, 0, st>>>(out, po, pl, pm, NH, hs, S);
-    return status_from(cudaGetLastError());
+    return status_from(launch_k(attn_merge_kernel<OT>, dim3(B * NH), dim3(((hs + 31) / 32) * 32), 0, st, false, out, po, pl, pm, NH, hs, S));
 }
 
 extern "C" {
@@ -532,34 +531,30 @@ int gpt2b_kv_cache_write_f32(float* kv_cache, const float* qkv, int B, int NH, i
                              gpt2b_stream_t stream) {
     if (B <= 0 || NH <= 0 || hs <= 0 || maxT <= 0 || !kv_cache || !qkv || !d_pos) return GPT2B_ERR_INVALID_ARG;
     const int n = B * NH * hs;
-    kv_write_kernel<float><<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(kv_cache, qkv, B, NH, hs, maxT, d_pos);
-    return status_from(cudaGetLastError());
+    return status_from(launch_k(kv_write_kernel<float>, dim3((n + 255) / 256), dim3(256), 0, (cudaStream_t)stream, false, kv_cache, qkv, B, NH, hs, maxT, d_pos));
 }
 int gpt2b_kv_cache_write_bf16(uint16_t* kv_cache, const uint16_t* qkv, int B, int NH, int hs, int maxT,
                               const int* d_pos, gpt2b_stream_t stream) {
     if (B <= 0 || NH <= 0 || hs <= 0 || maxT <= 0 || !kv_cache || !qkv || !d_pos) return GPT2B_ERR_INVALID_ARG;
     const int n = B * NH * hs;
-    kv_write_kernel<__nv_bfloat16><<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(
-        (__nv_bfloat16*)kv_cache, (const __nv_bfloat16*)qkv, B, NH, hs, maxT, d_pos);
-    return status_from(cudaGetLastError());
+    return status_from(launch_k(kv_write_kernel<__nv_bfloat16>, dim3((n + 255) / 256), dim3(256), 0, (cudaStream_t)stream, false, 
+        (__nv_bfloat16*)kv_cache, (const __nv_bfloat16*)qkv, B, NH, hs, maxT, d_pos));
 }
 int gpt2b_kv_cache_write_w8_i8(uint8_t* kv_cache, float* kv_scale, const uint16_t* qkv, int B, int NH, int hs,
                                int maxT, const int* d_pos, gpt2b_stream_t stream) {
     if (B <= 0 || NH <= 0 || hs <= 0 || maxT <= 0 || !kv_cache || !kv_scale || !qkv || !d_pos)
         return GPT2B_ERR_INVALID_ARG;
     const int rows = B * NH * 2;
-    kv_write_w8_kernel<KV_I8><<<(rows + 7) / 8, 256, 0, (cudaStream_t)stream>>>(
-        kv_cache, kv_scale, (const __nv_bfloat16*)qkv, B, NH, hs, maxT, d_pos);
-    return status_from(cudaGetLastError());
+    return status_from(launch_k(kv_write_w8_kernel<KV_I8>, dim3((rows + 7) / 8), dim3(256), 0, (cudaStream_t)stream, false, 
+        kv_cache, kv_scale, (const __nv_bfloat16*)qkv, B, NH, hs, maxT, d_pos));
 }
 int gpt2b_kv_cache_write_w8_fp8(uint8_t* kv_cache, float* kv_scale, const uint16_t* qkv, int B, int NH, int hs,
                                 int maxT, const int* d_pos, gpt2b_stream_t stream) {
     if (B <= 0 || NH <= 0 || hs <= 0 || maxT <= 0 || !kv_cache || !kv_scale || !qkv || !d_pos)
         return GPT2B_ERR_INVALID_ARG;
     const int rows = B * NH * 2;
-    kv_write_w8_kernel<KV_FP8><<<(rows + 7) / 8, 256, 0, (cudaStream_t)stream>>>(
-        kv_cache, kv_scale, (const __nv_bfloat16*)qkv, B, NH, hs, maxT, d_pos);
-    return status_from(cudaGetLastError());
+    return status_from(launch_k(kv_write_w8_kernel<KV_FP8>, dim3((rows + 7) / 8), dim3(256), 0, (cudaStream_t)stream, false, 
+        kv_cache, kv_scale, (const __nv_bfloat16*)qkv, B, NH, hs, maxT, d_pos));
 }
 
 int gpt2b_attention_forward_kv_small_f32(float* out, const float* qkv, const float* kv_cache, int B, int NH, int hs,

@@ -198,9 +198,10 @@ int sm_count();                   // SMs of the current device (cached per devic
 int max_dyn_smem();               // opt-in dynamic shared memory per block (cached per device)
 int status_from(cudaError_t e);   // 0 or GPT2B_ERR_CUDA + code
 
-// Raise a kernel's dynamic shared-memory limit to the device maximum, once per
-// device (bit d of *mask).  A single maximal setting keeps every launch and
-// every captured graph node valid whatever size it requests.
+// Raise a kernel's dynamic shared-memory limit to the device maximum (minus
+// the kernel's static shared memory), once per device (bit d of *mask).  A
+// single maximal setting keeps every launch and every captured graph node
+// valid whatever size it requests.
 template <typename Kernel>
 inline cudaError_t ensure_smem_limit(Kernel k, unsigned long long* mask) {
     int dev = 0;
@@ -208,7 +209,11 @@ inline cudaError_t ensure_smem_limit(Kernel k, unsigned long long* mask) {
     if (e != cudaSuccess) return e;
     const unsigned long long bit = 1ull << (dev & 63);
     if (*mask & bit) return cudaSuccess;
-    e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, max_dyn_smem());
+    cudaFuncAttributes fa;
+    e = cudaFuncGetAttributes(&fa, k);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             max_dyn_smem() - (int)fa.sharedSizeBytes);
     if (e == cudaSuccess) *mask |= bit;
     return e;
 }

@@ -612,8 +612,7 @@ int gpt2b_engine_generate(gpt2b_engine* e, const int* prompt, int n_prompt, int 
                     // replace the greedy pick by a softmax sample (step = position of the new token)
                     int rc = gpt2b_gpu_sample_softmax(e->d_token, e->logits, 1, V, seed, s + 1, (gpt2b_stream_t)st);
                     if (rc) return rc;
-                    set_history_kernel<<<1, 1, 0, st>>>(e->d_history, e->d_token, e->d_pos);
-                    err = cudaGetLastError();
+                    err = launch_k(set_history_kernel, dim3(1), dim3(1), 0, st, false, e->d_history, e->d_token, e->d_pos);
                 }
                 if (err == cudaSuccess && logits_host)
                     err = cudaMemcpyAsync(logits_host + (size_t)s * Vp, e->logits, (size_t)Vp * 4,

@@ -82,9 +82,8 @@ static int ln_entry(T* residual, T* normed, float* mean, float* rstd, const T* i
     if (N < 0 || C <= 0 || !normed || !in1 || !w || !b || (in2 && !residual)) return GPT2B_ERR_INVALID_ARG;
     if (C > kNormMaxPer * 32) return GPT2B_ERR_UNSUPPORTED;
     if (N == 0) return GPT2B_OK;
-    ln_rows_kernel<T><<<(N + kNormWarps - 1) / kNormWarps, kNormWarps * 32, 0, st>>>(residual, normed, mean, rstd,
-                                                                                    in1, in2, w, b, N, C);
-    return status_from(cudaGetLastError());
+    return status_from(launch_k(ln_rows_kernel<T>, dim3((N + kNormWarps - 1) / kNormWarps), dim3(kNormWarps * 32), 0, st, false, residual, normed, mean, rstd,
+                                                                                    in1, in2, w, b, N, C));
 }
 
 template <typename T>
@@ -92,8 +91,7 @@ static int enc_entry(T* out, const int* inp, const T* wte, const T* wpe, const i
                      cudaStream_t st) {
     if (B <= 0 || C <= 0 || !out || !inp || !wte || !wpe || !d_pos) return GPT2B_ERR_INVALID_ARG;
     dim3 grid((C + 255) / 256, B);
-    encoder_kv_kernel<T><<<grid, 256, 0, st>>>(out, inp, wte, wpe, d_pos, B, C, 0, 1 << 30);
-    return status_from(cudaGetLastError());
+    return status_from(launch_k(encoder_kv_kernel<T>, dim3(grid), dim3(256), 0, st, false, out, inp, wte, wpe, d_pos, B, C, 0, 1 << 30));
 }
 
 }  // namespace gpt2b

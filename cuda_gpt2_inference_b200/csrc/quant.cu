@@ -142,10 +142,13 @@ int gpt2b_quantize_buffer(const void* bf16_image, size_t nbytes, void* out8, flo
         const size_t n = lay.n[i];
         err = cudaMemcpy(d_in, src, n * 2, cudaMemcpyHostToDevice);
         if (err != cudaSuccess) break;
-        widen_bf16_kernel<<<4 * sm_count(), 256>>>(d_in, d_f, n);
-        if (fp8) quant_rows_kernel<true><<<lay.M[g], kQThreads>>>(d_f, d_q, d_s, lay.M[g], lay.K[g]);
-        else quant_rows_kernel<false><<<lay.M[g], kQThreads>>>(d_f, d_q, d_s, lay.M[g], lay.K[g]);
-        err = cudaGetLastError();
+        err = launch_k(widen_bf16_kernel, dim3(4 * sm_count()), dim3(256), 0, (cudaStream_t)0, false,
+                       (const uint16_t*)d_in, d_f, n);
+        if (err == cudaSuccess)
+            err = fp8 ? launch_k(quant_rows_kernel<true>, dim3(lay.M[g]), dim3(kQThreads), 0, (cudaStream_t)0, false,
+                                 (const float*)d_f, d_q, d_s, lay.M[g], lay.K[g])
+                      : launch_k(quant_rows_kernel<false>, dim3(lay.M[g]), dim3(kQThreads), 0, (cudaStream_t)0, false,
+                                 (const float*)d_f, d_q, d_s, lay.M[g], lay.K[g]);
         if (err == cudaSuccess) err = cudaMemcpy(dst, d_q, n, cudaMemcpyDeviceToHost);
         if (err == cudaSuccess) err = cudaMemcpy(scales + sc_off[g], d_s, (size_t)lay.M[g] * 4, cudaMemcpyDeviceToHost);
         dst += n;
@@ -191,25 +194,22 @@ int gpt2b_quantize_file(const char* in_bf16_path, const char* out8_path, const c
 int gpt2b_quant_rows_i8(const float* W, uint8_t* W8, float* scale, int M, int K, gpt2b_stream_t stream) {
     if (M < 0 || K <= 0 || !W || !W8 || !scale) return GPT2B_ERR_INVALID_ARG;
     if (M == 0) return GPT2B_OK;
-    quant_rows_kernel<false><<<M, kQThreads, 0, (cudaStream_t)stream>>>(W, W8, scale, M, K);
-    return status_from(cudaGetLastError());
+    return status_from(launch_k(quant_rows_kernel<false>, dim3(M), dim3(kQThreads), 0, (cudaStream_t)stream, false, W,
+                                W8, scale, M, K));
 }
 int gpt2b_quant_rows_fp8(const float* W, uint8_t* W8, float* scale, int M, int K, gpt2b_stream_t stream) {
     if (M < 0 || K <= 0 || !W || !W8 || !scale) return GPT2B_ERR_INVALID_ARG;
     if (M == 0) return GPT2B_OK;
-    quant_rows_kernel<true><<<M, kQThreads, 0, (cudaStream_t)stream>>>(W, W8, scale, M, K);
-    return status_from(cudaGetLastError());
+    return status_from(launch_k(quant_rows_kernel<true>, dim3(M), dim3(kQThreads), 0, (cudaStream_t)stream, false, W, W8, scale, M, K));
 }
 int gpt2b_dequant_wte_i8(const uint8_t* w8, const float* scale, uint16_t* out, int Vp, int C, gpt2b_stream_t stream) {
     if (Vp <= 0 || C <= 0 || !w8 || !scale || !out) return GPT2B_ERR_INVALID_ARG;
-    dequant_rows_kernel<false><<<4 * sm_count(), 256, 0, (cudaStream_t)stream>>>(w8, scale, (__nv_bfloat16*)out, Vp, C);
-    return status_from(cudaGetLastError());
+    return status_from(launch_k(dequant_rows_kernel<false>, dim3(4 * sm_count()), dim3(256), 0, (cudaStream_t)stream, false, w8, scale, (__nv_bfloat16*)out, Vp, C));
 }
 int gpt2b_dequant_wte_fp8(const uint8_t* w8, const float* scale, uint16_t* out, int Vp, int C,
                           gpt2b_stream_t stream) {
     if (Vp <= 0 || C <= 0 || !w8 || !scale || !out) return GPT2B_ERR_INVALID_ARG;
-    dequant_rows_kernel<true><<<4 * sm_count(), 256, 0, (cudaStream_t)stream>>>(w8, scale, (__nv_bfloat16*)out, Vp, C);
-    return status_from(cudaGetLastError());
+    return status_from(launch_k(dequant_rows_kernel<true>, dim3(4 * sm_count()), dim3(256), 0, (cudaStream_t)stream, false, w8, scale, (__nv_bfloat16*)out, Vp, C));
 }
 
 }  // extern "C"

@@ -125,14 +125,12 @@ extern "C" {
 int gpt2b_gpu_sample_softmax(int* d_token, const float* logits, int B, int V, unsigned long long seed, int step,
                              gpt2b_stream_t stream) {
     if (B <= 0 || V <= 0 || !d_token || !logits) return GPT2B_ERR_INVALID_ARG;
-    sample_softmax_kernel<<<B, kSampThreads, 0, (cudaStream_t)stream>>>(d_token, logits, B, V, seed, step);
-    return status_from(cudaGetLastError());
+    return status_from(launch_k(sample_softmax_kernel, dim3(B), dim3(kSampThreads), 0, (cudaStream_t)stream, false, d_token, logits, B, V, seed, step));
 }
 
 int gpt2b_gpu_argmax(int* d_token, const float* logits, int B, int V, int ld, gpt2b_stream_t stream) {
     if (B <= 0 || V <= 0 || ld < V || !d_token || !logits) return GPT2B_ERR_INVALID_ARG;
-    argmax_kernel<<<B, kArgThreads, 0, (cudaStream_t)stream>>>(d_token, logits, V, ld);
-    return status_from(cudaGetLastError());
+    return status_from(launch_k(argmax_kernel, dim3(B), dim3(kArgThreads), 0, (cudaStream_t)stream, false, d_token, logits, V, ld));
 }
 
 }  // extern "C"
