@@ -78,6 +78,7 @@ _SIGS = {
     "gpt2b_attention_kv_split_bf16": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
     "gpt2b_attention_kv_merge_bf16": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "gpt2b_attention_kv_merge_f32": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P]),
+    "gpt2b_attention_forward_kv_large_bf16_noalloc": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _I, _P]),
     "gpt2b_layernorm_forward_f32": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _P]),
     "gpt2b_layernorm_forward_bf16": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _P]),
     "gpt2b_fused_residual_forward5_f32": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _P]),

@@ -24,6 +24,7 @@
 #include "internal.h"
 
 #include <float.h>
+#include <mutex>
 
 namespace gpt2b {
 
@@ -629,3 +630,66 @@ int gpt2b_attention_kv_merge_f32(float* out, const float* part_out, const float*
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free split+merge attention (BF16 KV)
+// ---------------------------------------------------------------------------
+// Some callers cannot hand this library a scratch buffer: a host that owns
+// every byte of device memory through its own pool and forbids side
+// allocations, or code on a latency-critical path where cudaMalloc's implicit
+// device synchronisation is not acceptable.  For them the split partials of
+// the flash-decoding attention live in a fixed array inside this library
+// instead of caller memory.  The array is sized for kNoAllocMaxSlots
+// (batch x heads x splits) partial rows; every GPU that loads the library
+// keeps it (about 0.5 MB) until the process exits.
+namespace gpt2b {
+
+constexpr int kNoAllocMaxSlots = 2048;  // B * NH * S limit of the allocation-free entry point
+
+// [part_out: kNoAllocMaxSlots * 64 floats][part_max: kNoAllocMaxSlots][part_lse: kNoAllocMaxSlots]
+static __device__ __align__(256) float g_noalloc_partials[kNoAllocMaxSlots * (kHS + 2)];
+
+// Host code must not pass &g_noalloc_partials to a kernel: on the host that
+// name is only a stand-in, not the device address.  The device address is
+// looked up once per device with that device current and cached here.
+static float* g_noalloc_dev_ptr[64] = {nullptr};
+static std::mutex g_noalloc_mu;
+
+static int noalloc_partials_ptr(float** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return status_from(e);
+    if (dev < 0 || dev >= 64) return GPT2B_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_dev_ptr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_partials);
+        if (e != cudaSuccess) return status_from(e);
+        g_noalloc_dev_ptr[dev] = static_cast<float*>(p);
+    }
+    *out = g_noalloc_dev_ptr[dev];
+    return GPT2B_OK;
+}
+
+}  // namespace gpt2b
+
+extern "C" int gpt2b_attention_forward_kv_large_bf16_noalloc(uint16_t* out, const uint16_t* qkv,
+                                                             const uint16_t* kv_cache, int B, int NH, int hs,
+                                                             int maxT, const int* d_pos, int S,
+                                                             gpt2b_stream_t stream) {
+    if (B <= 0 || NH <= 0 || S <= 0) return GPT2B_ERR_INVALID_ARG;
+    if ((long long)B * NH * S > kNoAllocMaxSlots) return GPT2B_ERR_INVALID_ARG;  // beyond the built-in scratch
+    float* base = nullptr;
+    int rc = noalloc_partials_ptr(&base);
+    if (rc) return rc;
+    // Every partial slot the merge reads is written by the split kernel of the
+    // same call (empty splits write neutral values), so nothing is cleared.
+    float* part_out = base;
+    float* part_max = base + (size_t)kNoAllocMaxSlots * kHS;
+    float* part_lse = part_max + kNoAllocMaxSlots;
+    rc = attn_split(KV_BF16, part_out, part_lse, part_max, qkv, kv_cache, nullptr, B, NH, hs, maxT, S, d_pos,
+                    (cudaStream_t)stream);
+    return rc ? rc
+              : attn_merge<__nv_bfloat16>((__nv_bfloat16*)out, part_out, part_lse, part_max, B, NH, hs, S,
+                                          (cudaStream_t)stream);
+}

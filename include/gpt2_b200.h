@@ -184,6 +184,20 @@ int gpt2b_attention_kv_merge_bf16(uint16_t* out, const float* part_out, const fl
                                   const float* part_max, int B, int NH, int hs, int S, gpt2b_stream_t stream);
 int gpt2b_attention_kv_merge_f32(float* out, const float* part_out, const float* part_lse, const float* part_max,
                                  int B, int NH, int hs, int S, gpt2b_stream_t stream);
+/* No counterpart in the reference.  gpt2b_attention_forward_kv_large_bf16
+ * without the three caller-provided partial buffers, for callers that cannot
+ * allocate device memory (a host whose memory pool owns the whole device, or a
+ * hot path that must not pay cudaMalloc's implicit synchronisation).  The split
+ * partials live in a fixed array inside the library (about 0.5 MB per GPU,
+ * held until the process exits): B*NH*S must not exceed 2048, else
+ * GPT2B_ERR_INVALID_ARG.  Allocates nothing.  The first call on a device looks
+ * up that array's device address (cudaGetSymbolAddress), so make that first
+ * call before any stream capture.  All calls share the one array: calls that
+ * can overlap on the GPU (different streams, or different host threads on the
+ * same device) race and must be serialised by the caller. */
+int gpt2b_attention_forward_kv_large_bf16_noalloc(uint16_t* out, const uint16_t* qkv, const uint16_t* kv_cache, int B,
+                                                  int NH, int hs, int maxT, const int* d_pos, int S,
+                                                  gpt2b_stream_t stream);
 
 /* ======================================================================== */
 /* LayerNorm, residual, embedding                                            */
