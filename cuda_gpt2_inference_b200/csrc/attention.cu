@@ -18,8 +18,9 @@
 //   ENGINE  the decode engine: K/V staging issued before griddepcontrol.wait
 //           (rows < pos were written by earlier tokens), the CTA that owns
 //           position pos appends the current token's K/V (quantising for 8-bit
-//           KV) to global memory and to its staged copy, and the last CTA of a
-//           head to finish merges the partials (no separate merge launch).
+//           KV) to global memory and to its staged copy, and every CTA writes
+//           its split partials; the projection GEMV that follows merges them in
+//           its prologue, so no merge launch, atomic or fence is needed here.
 #include "common.cuh"
 #include "internal.h"
 
@@ -118,7 +119,7 @@ struct AttnSmem {
     static constexpr int kStageBytes = 2 * kCH * kRowB + (k8 ? 2 * kScaleSlots * 4 : 0);
     static constexpr int kAccBytes = kRPP * kHS * 4;
     static constexpr int kBytes = 2 * kStageBytes + kAccBytes + kHS * 4 /*q*/ + kCH * 4 /*p*/ + 64 /*red*/ +
-                                  32 /*bars*/ + 16 /*flags*/;
+                                  32 /*bars*/;
 };
 
 struct AttnArgs {
@@ -126,7 +127,6 @@ struct AttnArgs {
     float* part_out;        // SPLIT / ENGINE partials
     float* part_max;
     float* part_lse;
-    unsigned* counters;     // ENGINE: one per head
     const void* qkv;
     void* kv;               // cache (layer base)
     float* kv_scale;        // 8-bit scales (layer base)
@@ -185,7 +185,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
     float* p_s = q_s + kHS;
     float* red = p_s + S::kCH;
     uint64_t* bars = reinterpret_cast<uint64_t*>(red + 16);
-    int* flags = reinterpret_cast<int*>(bars + 4);
 
     const int tid = threadIdx.x;
     const int NH = a.NH, maxT = a.maxT;
@@ -209,11 +208,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
         const int chunk = (total + nsplit - 1) / nsplit;  // attention_kvcache.cuh:197-199
         j0 = s * chunk; j1 = min(j0 + chunk, total);
     } else {
-        // engine chunking: multiples of 16 positions, at most CH per CTA
-        int chunk = (total + nsplit - 1) / nsplit;
-        chunk = max(16, (chunk + 15) & ~15);
+        // engine chunking: multiples of 16 positions, at most CH per CTA; the
+        // merging GEMV prologue derives the same split count from the position
+        const int chunk = engine_attn_chunk(total, nsplit);
         j0 = s * chunk; j1 = min(j0 + chunk, total);
-        nsplit = (total + chunk - 1) / chunk;  // splits that have work
     }
     const int n_local = j1 - j0;
     const size_t bh = (size_t)b * NH + h;
@@ -396,35 +394,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
     if (tid < kHS)
         for (int g = 0; g < S::kRPP; g++) o += accbuf[g * kHS + tid];
 
-    if (MODE == AM_SINGLE || (MODE == AM_ENGINE && nsplit == 1)) {
+    if (MODE == AM_SINGLE) {
         if (tid < kHS) reinterpret_cast<XT*>(a.out)[bh * kHS + tid] = from_f<XT>(o / l_run);
         return;
     }
-    const int S_slots = a.S;
-    const size_t slot = bh * S_slots + s;
+    // SPLIT and ENGINE: per-split partials (the engine's projection GEMV merges
+    // them in its prologue, PRO_ATTN_MERGE)
+    const size_t slot = bh * a.S + s;
     if (tid < kHS) a.part_out[slot * kHS + tid] = o;
     if (tid == 0) { a.part_max[slot] = m_run; a.part_lse[slot] = l_run; }
-    if (MODE == AM_SPLIT) return;
-
-    // ENGINE: the last CTA of this head merges (attention_kvcache.cuh:298-318)
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) flags[1] = (atomicAdd(&a.counters[bh], 1u) == (unsigned)(nsplit - 1));
-    __syncthreads();
-    if (!flags[1]) return;
-    __threadfence();
-    if (tid < kHS) {
-        float mg = -FLT_MAX;
-        for (int k = 0; k < nsplit; k++) mg = fmaxf(mg, __ldcg(&a.part_max[bh * S_slots + k]));
-        float of = 0.0f, lf = 0.0f;
-        for (int k = 0; k < nsplit; k++) {
-            const float rs = __expf(__ldcg(&a.part_max[bh * S_slots + k]) - mg);
-            of += rs * __ldcg(&a.part_out[(bh * S_slots + k) * kHS + tid]);
-            lf += rs * __ldcg(&a.part_lse[bh * S_slots + k]);
-        }
-        reinterpret_cast<XT*>(a.out)[bh * kHS + tid] = from_f<XT>(of / lf);
-    }
-    if (tid == 0) a.counters[bh] = 0u;
 }
 
 // LSE merge of S partials (attention_kvcache.cuh:298-318).
@@ -470,12 +448,11 @@ static cudaError_t launch_attn_kind(int kv, const AttnArgs& a, int grid, cudaStr
 
 int attn_engine_max_chunk(int kv) { return kv == KV_F32 ? KvT<KV_F32>::kCH : KvT<KV_BF16>::kCH; }
 
-cudaError_t launch_attention_engine(int kv, void* atty, const void* qkv, void* kv_layer, float* kv_scale_layer,
-                                    const int* d_pos, int NH, int maxT, int splits, float* part_out,
-                                    float* part_max, float* part_lse, unsigned* counters, cudaStream_t st,
-                                    bool pdl) {
+cudaError_t launch_attention_engine(int kv, const void* qkv, void* kv_layer, float* kv_scale_layer, const int* d_pos,
+                                    int NH, int maxT, int splits, float* part_out, float* part_max, float* part_lse,
+                                    cudaStream_t st, bool pdl) {
     AttnArgs a{};
-    a.out = atty; a.part_out = part_out; a.part_max = part_max; a.part_lse = part_lse; a.counters = counters;
+    a.part_out = part_out; a.part_max = part_max; a.part_lse = part_lse;
     a.qkv = qkv; a.kv = kv_layer; a.kv_scale = kv_scale_layer; a.d_pos = d_pos;
     a.B = 1; a.NH = NH; a.maxT = maxT; a.S = splits; a.scale = 1.0f / sqrtf((float)kHS);
     return launch_attn_kind<AM_ENGINE>(kv, a, NH * splits, st, pdl);

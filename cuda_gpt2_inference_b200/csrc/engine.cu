@@ -53,7 +53,6 @@ struct gpt2b_engine {
     unsigned char *encoded, *ln1, *qkv, *atty, *res2, *ln2, *fch, *fch_gelu, *res3, *lnf, *proj_out, *fcproj_out;
     float* logits;
     float *part_out, *part_max, *part_lse;
-    unsigned* attn_counters;
     float* lm_val;
     int* lm_idx;
     unsigned* lm_counter;
@@ -137,11 +136,10 @@ cudaError_t launch_step(gpt2b_engine* e) {
         if (err != cudaSuccess) return err;
         unsigned char* kv_l = e->kv_cache + (size_t)l * e->kv_layer_elems * (e->kvk >= KV_I8 ? 1 : e->xbytes);
         float* ks_l = e->kv_scale ? e->kv_scale + (size_t)l * e->kv_layer_scales : nullptr;
-        err = launch_attention_engine(e->kvk, e->atty + (size_t)l * e->cfg.channels * e->xbytes, e->qkv, kv_l, ks_l,
-                                      e->d_pos, e->cfg.num_heads, e->cfg.max_seq_len, e->splits, e->part_out,
-                                      e->part_max, e->part_lse, e->attn_counters, e->stream, pdl);
+        err = launch_attention_engine(e->kvk, e->qkv, kv_l, ks_l, e->d_pos, e->cfg.num_heads, e->cfg.max_seq_len,
+                                      e->splits, e->part_out, e->part_max, e->part_lse, e->stream, pdl);
         if (err != cudaSuccess) return err;
-        err = launch_gemv(e->proj_p[l], e->wk, false, PRO_PLAIN, EPI_STORE, e->stream, pdl);
+        err = launch_gemv(e->proj_p[l], e->wk, false, PRO_ATTN_MERGE, EPI_STORE, e->stream, pdl);
         if (err != cudaSuccess) return err;
         err = launch_gemv(e->fc_p[l], e->wk, false, PRO_RES_LN, EPI_STORE, e->stream, pdl);
         if (err != cudaSuccess) return err;
@@ -282,14 +280,14 @@ int build_engine(const unsigned char* image, size_t nbytes, const float* scales,
     e->splits = splits;
     const int lm_grid_max = 2 * nsm;
     struct Slot { unsigned char** ptr; size_t bytes; };
-    unsigned char *logits_b, *po_b, *pm_b, *pl_b, *cnt_b, *lmv_b, *lmi_b, *lmc_b, *tok_b, *pos_b, *hist_b, *pr_b, *np_b;
+    unsigned char *logits_b, *po_b, *pm_b, *pl_b, *lmv_b, *lmi_b, *lmc_b, *tok_b, *pos_b, *hist_b, *pr_b, *np_b;
     std::vector<Slot> slots = {
         {&e->encoded, C * xb},        {&e->ln1, (size_t)L * C * xb},   {&e->qkv, 3 * (size_t)C * xb},
         {&e->atty, (size_t)L * C * xb}, {&e->res2, (size_t)L * C * xb}, {&e->ln2, (size_t)L * C * xb},
         {&e->fch, (size_t)L * 4 * C * xb}, {&e->fch_gelu, 4 * (size_t)C * xb}, {&e->res3, (size_t)L * C * xb},
         {&e->lnf, C * xb},            {&e->proj_out, C * xb},          {&e->fcproj_out, C * xb},
         {&logits_b, (size_t)Vp * 4},  {&po_b, (size_t)NH * splits * hs * 4}, {&pm_b, (size_t)NH * splits * 4},
-        {&pl_b, (size_t)NH * splits * 4}, {&cnt_b, (size_t)NH * 4},   {&lmv_b, (size_t)lm_grid_max * 4},
+        {&pl_b, (size_t)NH * splits * 4}, {&lmv_b, (size_t)lm_grid_max * 4},
         {&lmi_b, (size_t)lm_grid_max * 4}, {&lmc_b, 16},               {&tok_b, 16},
         {&pos_b, 16},                 {&hist_b, (size_t)(maxT + 1) * 4}, {&pr_b, (size_t)maxT * 4},
         {&np_b, 16}};
@@ -304,7 +302,6 @@ int build_engine(const unsigned char* image, size_t nbytes, const float* scales,
     e->part_out = reinterpret_cast<float*>(po_b);
     e->part_max = reinterpret_cast<float*>(pm_b);
     e->part_lse = reinterpret_cast<float*>(pl_b);
-    e->attn_counters = reinterpret_cast<unsigned*>(cnt_b);
     e->lm_val = reinterpret_cast<float*>(lmv_b);
     e->lm_idx = reinterpret_cast<int*>(lmi_b);
     e->lm_counter = reinterpret_cast<unsigned*>(lmc_b);
@@ -364,7 +361,14 @@ int build_engine(const unsigned char* image, size_t nbytes, const float* scales,
         pr.W = e->p[6] + (size_t)l * C * C * wb;
         pr.scale = w8 ? e->sc[2] + (size_t)l * C : nullptr;
         pr.bias = e->p[7] + (size_t)l * C * xb;
-        pr.x = e->atty + (size_t)l * C * xb;
+        pr.part_out = e->part_out;  // x = merge of the attention partials (PRO_ATTN_MERGE)
+        pr.part_max = e->part_max;
+        pr.part_lse = e->part_lse;
+        pr.attn_heads = NH;
+        pr.attn_splits = splits;
+        pr.d_pos = e->d_pos;
+        pr.atty_out = e->atty + (size_t)l * C * xb;
+        pr.aux_bytes = NH * splits * 64 * 4 + 2 * (((NH * splits * 4) + 15) & ~15);
         pr.out = e->proj_out;
         pr.M = C; pr.K = C;
         plan_gemv(pr, wk, nsm, true);

@@ -1,43 +1,72 @@
 // gemv.cu -- batch-1 decode GEMVs for FP32 / BF16 / INT8 / FP8 weights.
 //
-// Design (B200, HBM-bound, no tensor cores: one activation vector is not a
-// dense contraction):
-//   * A CTA owns whole row tiles.  Rows of a row-major matrix are contiguous,
-//     so a tile is one contiguous byte range that a single elected thread moves
-//     into shared memory with one cp.async.bulk, completing on an mbarrier.
-//     The whole matrix is in flight at once for the per-layer shapes (one tile
-//     per CTA, tiles sized to spread the bytes evenly over the 148 SMs); large
-//     matrices (LM head) stream through a 2-3 stage ring.
-//   * The weight copies are issued before griddepcontrol.wait, so under
-//     programmatic dependent launch a GEMV fetches its weights while the
-//     kernel before it is still running; only the activation vector waits.
-//   * Each warp takes a pair of rows (x is read once per pair) and, when a
-//     tile has fewer than 16 rows, a slice of K so all 8 warps work; FP32
-//     accumulation, shuffle reduction, then bias / GELU / pre-GELU epilogue.
-//   * Fused prologues for the engine: residual add + LayerNorm (or embedding
-//     lookup + LayerNorm) computed redundantly per CTA from ~3 KB of L2-resident
-//     data, which removes the separate LN kernels of the reference.
-//   * Fused LM-head epilogue: logits, per-CTA argmax, last-CTA reduction and
-//     device-side token/position advance (greedy decode without host trips).
+// Design (B200, HBM/latency-bound, no tensor cores: one activation vector is
+// not a dense contraction):
+//   * Warp specialisation: one producer warp streams row tiles of W into a
+//     shared-memory ring with cp.async.bulk (rows of a row-major matrix are
+//     contiguous, so a tile is one contiguous byte range, plus its 8-bit row
+//     scales), completing on per-stage "full" mbarriers; eight consumer warps
+//     compute and release stages through "empty" mbarriers.  No block-wide
+//     barrier sits in the streaming loop.
+//   * Per-layer matrices use one tile per CTA sized to spread the bytes over
+//     the SMs, so the whole matrix is in flight at once; the LM head streams
+//     ~24 KB tiles through up to 8 stages per SM.
+//   * Programmatic dependent launch: the producer never waits on the previous
+//     kernel (weights are immutable), and consumers prefetch every parameter
+//     they will need (LayerNorm gamma/beta, bias, row scales) before
+//     griddepcontrol.wait.  After the wait the activation vector arrives in one
+//     round trip (all 16-byte loads in flight, or bulk copies for the
+//     attention partials).
+//   * Each consumer warp takes a pair of rows (x read once per pair) and, when a
+//     tile has fewer than 16 rows, a slice of K.  FP32 accumulation; INT8 and
+//     E4M3 codes decode exactly with integer/bit operations (common.cuh).
+//   * Fused prologues for the engine: residual add + LayerNorm, embedding +
+//     LayerNorm, or the LSE merge of the attention split partials -- computed
+//     redundantly per CTA from a few KB of L2-resident data instead of separate
+//     launches.  Fused LM-head epilogue: logits, per-CTA argmax, last-CTA pick,
+//     device-side token/position advance.
 #include "common.cuh"
 #include "internal.h"
 
 #include <float.h>
+#include <stdlib.h>
 
 namespace gpt2b {
 
 GPT2B_DEFINE_ERROR_READER(gemv_device_error)
 
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
-constexpr int kRedFloats = 160;  // per-warp partial sums (>= rows per tile + 16)
-constexpr int kMaxLnPer = 8;     // LayerNorm prologue: C <= 8 * 256
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumers = kConsumerWarps * 32;
+constexpr int kThreads = kConsumers + 32;  // + one producer warp
+constexpr int kMaxStages = 8;              // ring depth of kernel A
+constexpr int kMaxWarpStages = 4;          // per-warp ring depth of kernel B
+constexpr int kRedFloats = 160;            // per-slot partial sums (>= rows per tile + 16)
+constexpr int kLnChunks = 2;               // 16-byte LayerNorm chunks per consumer thread (C <= 2048)
+constexpr int kBarBytes = 512;             // mbarriers (kernel B: 8 warps x 4 stages + 1)
+constexpr int kSmemHeader = kBarBytes + kRedFloats * 4 + 64;
 
 template <int WK> struct WTraits;
-template <> struct WTraits<WK_F32> { using XT = float; static constexpr int kElemsPerChunk = 4; };
-template <> struct WTraits<WK_BF16> { using XT = __nv_bfloat16; static constexpr int kElemsPerChunk = 8; };
-template <> struct WTraits<WK_I8> { using XT = __nv_bfloat16; static constexpr int kElemsPerChunk = 16; };
-template <> struct WTraits<WK_FP8> { using XT = __nv_bfloat16; static constexpr int kElemsPerChunk = 16; };
+template <> struct WTraits<WK_F32> { using XT = float; };
+template <> struct WTraits<WK_BF16> { using XT = __nv_bfloat16; };
+template <> struct WTraits<WK_I8> { using XT = __nv_bfloat16; };
+template <> struct WTraits<WK_FP8> { using XT = __nv_bfloat16; };
+
+// consumer-only barrier (named barrier 1, the 8 consumer warps)
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+// all-reduce over the 256 consumer threads through `scratch` (>= 8 floats)
+__device__ __forceinline__ float consumer_sum(float v, float* scratch) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    v = warp_sum(v);
+    if (lane == 0) scratch[w] = v;
+    consumer_sync();
+    float t = (lane < kConsumerWarps) ? scratch[lane] : 0.0f;
+    t = warp_sum(t);
+    consumer_sync();
+    return t;
+}
 
 // Dot product of one 16-byte weight chunk of two rows with the matching x.
 template <int WK>
@@ -86,66 +115,149 @@ __device__ __forceinline__ void chunk_dot2(const uint4& w0, const uint4& w1, con
     }
 }
 
-// Decoded value of element c of embedding row `tok` (PRO_EMB_LN): the
-// activation-type table, or the 8-bit code times its row scale rounded to
-// bf16 -- exactly what dequant_wte_kernel stores (GEMV_w8.cuh:396).
-template <int WK>
-__device__ __forceinline__ float emb_value(const GemvParams& p, int tok, int c) {
-    using XT = typename WTraits<WK>::XT;
+// 16 bytes of activations <-> E floats (E = 4 for float, 8 for bf16)
+template <typename XT> struct Vec;
+template <> struct Vec<float> {
+    static constexpr int E = 4;
+    __device__ static void unpack(const uint4& u, float* f) {
+        f[0] = __uint_as_float(u.x); f[1] = __uint_as_float(u.y); f[2] = __uint_as_float(u.z); f[3] = __uint_as_float(u.w);
+    }
+    __device__ static uint4 pack(const float* f) {
+        return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), __float_as_uint(f[3]));
+    }
+};
+template <> struct Vec<__nv_bfloat16> {
+    static constexpr int E = 8;
+    __device__ static void unpack(const uint4& u, float* f) {
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) { f[2 * i] = bf16lo(w[i]); f[2 * i + 1] = bf16hi(w[i]); }
+    }
+    __device__ static uint32_t pack2(float lo, float hi) {
+        const uint32_t l = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
+        const uint32_t h = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
+        return l | (h << 16);
+    }
+    __device__ static uint4 pack(const float* f) {
+        return make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
+    }
+};
+
+// Embedding chunk (8 or 4 values) of row `tok`, as dequant_wte_kernel stores it
+// for 8-bit tables (GEMV_w8.cuh:396): bf16(decode(code) * scale[row]).
+template <int WK, typename XT>
+__device__ __forceinline__ void emb_chunk(const GemvParams& p, int tok, int c, float* f) {
+    constexpr int E = Vec<XT>::E;
     if constexpr (WK == WK_I8 || WK == WK_FP8) {
-        const uint8_t code = p.wte8[(size_t)tok * p.K + c];
-        const float v = (WK == WK_I8) ? (float)(int8_t)code : e4m3_to_f((uint32_t)code, 0);
-        return round_to<__nv_bfloat16>(v * p.wte_scale[tok]);
+        const uint2 codes = *reinterpret_cast<const uint2*>(p.wte8 + (size_t)tok * p.K + (size_t)c * E);
+        const float s = p.wte_scale[tok];
+        const uint32_t cw[2] = {codes.x, codes.y};
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const uint32_t w = cw[i >> 2];
+            const float v = (WK == WK_I8) ? (float)(int8_t)((w >> (8 * (i & 3))) & 0xffu) : e4m3_to_f(w, i & 3);
+            f[i] = round_to<__nv_bfloat16>(v * s);
+        }
     } else {
-        return to_f<XT>(reinterpret_cast<const XT*>(p.wte)[(size_t)tok * p.K + c]);
+        const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const XT*>(p.wte) + (size_t)tok * p.K +
+                                                        (size_t)c * E);
+        Vec<XT>::unpack(u, f);
     }
 }
 
-template <int WK, typename OT, int PRO, int EPI>
-__global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
+// LayerNorm gamma/beta chunks a consumer thread will need (prefetched before
+// griddepcontrol.wait: parameters never depend on the previous kernel).
+template <int WK, int PRO>
+__device__ __forceinline__ void prefetch_ln_params(const GemvParams& p, uint4* lw, uint4* lb) {
     using XT = typename WTraits<WK>::XT;
-    constexpr int kWB = (WK == WK_F32) ? 4 : (WK == WK_BF16 ? 2 : 1);
-    extern __shared__ __align__(16) unsigned char smem[];
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem);            // 4 stages max
-    float* red = reinterpret_cast<float*>(smem + 64);               // kRedFloats
-    unsigned char* xs = smem + 64 + kRedFloats * 4;                 // K activations
-    const int x_bytes = ((p.K * (int)sizeof(XT)) + 15) & ~15;
-    unsigned char* stages = xs + x_bytes;
-
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const size_t row_bytes = (size_t)p.K * kWB;
-    const int R = p.rows_per_tile, NS = p.nstages, G = gridDim.x;
-    const unsigned char* Wb = reinterpret_cast<const unsigned char*>(p.W);
-
-    // ---- 1. stage the first tiles (weights never depend on other kernels) ----
-    if (tid == 0) {
-        for (int s = 0; s < NS; s++) mbar_init(&bars[s], 1);
-        mbar_fence_init();
-    }
-    __syncthreads();
-    if (tid == 0) {
-        for (int s = 0; s < NS; s++) {
-            const int t = blockIdx.x + s * G;
-            if (t >= p.ntiles) break;
-            const int r0 = t * R, nr = min(R, p.M - r0);
-            const uint32_t bytes = (uint32_t)(nr * row_bytes);
-            mbar_arrive_expect_tx(&bars[s], bytes);
-            bulk_g2s(stages + (size_t)s * p.tile_bytes, Wb + (size_t)r0 * row_bytes, bytes, &bars[s]);
+    if constexpr (PRO == PRO_RES_LN || PRO == PRO_EMB_LN) {
+        const int tid = threadIdx.x, nch = p.K / Vec<XT>::E;
+#pragma unroll
+        for (int j = 0; j < kLnChunks; j++) {
+            const int c = tid + j * kConsumers;
+            if (c < nch) {
+                lw[j] = reinterpret_cast<const uint4*>(p.ln_w)[c];
+                lb[j] = reinterpret_cast<const uint4*>(p.ln_b)[c];
+            }
         }
     }
+}
 
-    // ---- 2. wait for the producer of x, then let the next kernel launch ----
-    pdl_wait();
-    pdl_trigger();
-
-    // ---- 3. x into shared memory (plain, or residual/embedding + LayerNorm) ----
-    XT* xsv = reinterpret_cast<XT*>(xs);
+// The activation vector x (K values) into shared memory, run by the 256
+// consumer threads after griddepcontrol.wait: a plain copy with every 16-byte
+// load in flight at once, the LSE merge of the attention partials (staged by
+// bulk copies), or residual/embedding + LayerNorm.  Ends with a consumer
+// barrier.  Returns false if a bounded wait gave up.
+template <int WK, int PRO>
+__device__ bool build_x(const GemvParams& p, unsigned char* xs, unsigned char* aux, uint64_t* aux_bar, float* misc,
+                        const uint4* lw, const uint4* lb) {
+    using XT = typename WTraits<WK>::XT;
+    constexpr int E = Vec<XT>::E;
+    const int tid = threadIdx.x;
+    const int x_bytes = ((p.K * (int)sizeof(XT)) + 15) & ~15;
     if constexpr (PRO == PRO_PLAIN) {
-        const XT* x = reinterpret_cast<const XT*>(p.x);
-        for (int k = tid; k < p.K; k += kThreads) xsv[k] = x[k];
+        if (p.x_vec) {
+            const int nvec = x_bytes / 16;
+            const uint4* xv = reinterpret_cast<const uint4*>(p.x);
+            uint4* xd = reinterpret_cast<uint4*>(xs);
+            for (int base = 0; base < nvec; base += 4 * kConsumers) {
+                uint4 r[4];
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int i = base + j * kConsumers + tid;
+                    if (i < nvec) r[j] = xv[i];
+                }
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int i = base + j * kConsumers + tid;
+                    if (i < nvec) xd[i] = r[j];
+                }
+            }
+        } else {
+            const XT* x = reinterpret_cast<const XT*>(p.x);
+            XT* xd = reinterpret_cast<XT*>(xs);
+            for (int k = tid; k < p.K; k += kConsumers) xd[k] = x[k];
+        }
+    } else if constexpr (PRO == PRO_ATTN_MERGE) {
+        // stage all split partials with three bulk copies, then merge
+        // (attention_kvcache.cuh:298-318): o = sum e^{m_s-M} o_s / sum e^{m_s-M} l_s
+        const int NH = p.attn_heads, S = p.attn_splits;
+        const uint32_t ob = (uint32_t)(NH * S * 64 * 4);
+        const uint32_t mb = (uint32_t)(((NH * S * 4) + 15) & ~15);
+        float* po = reinterpret_cast<float*>(aux);
+        float* pm = reinterpret_cast<float*>(aux + ob);
+        float* pl = reinterpret_cast<float*>(aux + ob + mb);
+        if (tid == 0) {
+            mbar_arrive_expect_tx(aux_bar, ob + 2 * mb);
+            bulk_g2s(po, p.part_out, ob, aux_bar);
+            bulk_g2s(pm, p.part_max, mb, aux_bar);
+            bulk_g2s(pl, p.part_lse, mb, aux_bar);
+        }
+        const int total = *p.d_pos + 1;
+        const int chunk = engine_attn_chunk(total, S);
+        const int s_eff = min(S, (total + chunk - 1) / chunk);
+        if (!mbar_wait(aux_bar, 0)) return false;
+        XT* xd = reinterpret_cast<XT*>(xs);
+        for (int idx = tid; idx < NH * 64; idx += kConsumers) {
+            const int h = idx >> 6, d = idx & 63;
+            float m = -FLT_MAX;
+            for (int s = 0; s < s_eff; s++) m = fmaxf(m, pm[h * S + s]);
+            float o = 0.0f, l = 0.0f;
+            for (int s = 0; s < s_eff; s++) {
+                const float r = __expf(pm[h * S + s] - m);
+                o += r * po[(h * S + s) * 64 + d];
+                l += r * pl[h * S + s];
+            }
+            const XT v = from_f<XT>(o / l);
+            xd[idx] = v;
+            if (blockIdx.x == 0 && p.atty_out) reinterpret_cast<XT*>(p.atty_out)[idx] = v;
+        }
     } else {
-        const int C = p.K;
-        float v[kMaxLnPer];
+        // residual add (or embedding) + LayerNorm, two-pass like the reference
+        // (layernorm.cuh:171-241): the sum is rounded to the storage type and
+        // the statistics are taken over the rounded values.
+        const int C = p.K, nch = C / E;
+        float v[kLnChunks][E];
         float sum = 0.0f;
         int tok = 0, pos = 0;
         if constexpr (PRO == PRO_EMB_LN) {
@@ -154,62 +266,222 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
             if (tok < 0 || tok >= p.vocab) { if (tid == 0) report_device_error(GPT2B_DEVERR_BAD_TOKEN); tok = 0; }
             if (pos < 0 || pos >= p.maxT) { if (tid == 0) report_device_error(GPT2B_DEVERR_BAD_POS); pos = 0; }
         }
+        uint4 ra[kLnChunks], rb[kLnChunks];
 #pragma unroll
-        for (int i = 0; i < kMaxLnPer; i++) {
-            const int c = tid + i * kThreads;
-            float r = 0.0f;
-            if (c < C) {
+        for (int j = 0; j < kLnChunks; j++) {  // issue every load before using any
+            const int c = tid + j * kConsumers;
+            if (c < nch) {
                 if constexpr (PRO == PRO_EMB_LN) {
-                    r = emb_value<WK>(p, tok, c) + to_f<XT>(reinterpret_cast<const XT*>(p.wpe)[(size_t)pos * C + c]);
+                    rb[j] = reinterpret_cast<const uint4*>(reinterpret_cast<const XT*>(p.wpe) + (size_t)pos * C)[c];
                 } else {
-                    r = to_f<XT>(reinterpret_cast<const XT*>(p.res_in)[c]) +
-                        to_f<XT>(reinterpret_cast<const XT*>(p.delta)[c]);
+                    ra[j] = reinterpret_cast<const uint4*>(p.res_in)[c];
+                    rb[j] = reinterpret_cast<const uint4*>(p.delta)[c];
                 }
-                r = round_to<XT>(r);  // the residual is stored as floatX and LN reads it back
-                if (blockIdx.x == 0 && p.res_out) reinterpret_cast<XT*>(p.res_out)[c] = from_f<XT>(r);
-                sum += r;
             }
-            v[i] = r;
         }
-        const float mean = block_sum(sum, red) / (float)C;
+#pragma unroll
+        for (int j = 0; j < kLnChunks; j++) {
+            const int c = tid + j * kConsumers;
+#pragma unroll
+            for (int e = 0; e < E; e++) v[j][e] = 0.0f;
+            if (c < nch) {
+                float a[E], b[E];
+                if constexpr (PRO == PRO_EMB_LN) emb_chunk<WK, XT>(p, tok, c, a);
+                else Vec<XT>::unpack(ra[j], a);
+                Vec<XT>::unpack(rb[j], b);
+#pragma unroll
+                for (int e = 0; e < E; e++) {
+                    v[j][e] = round_to<XT>(a[e] + b[e]);
+                    sum += v[j][e];
+                }
+                if (blockIdx.x == 0 && p.res_out) reinterpret_cast<uint4*>(p.res_out)[c] = Vec<XT>::pack(v[j]);
+            }
+        }
+        const float mean = consumer_sum(sum, misc) / (float)C;
         float sq = 0.0f;
 #pragma unroll
-        for (int i = 0; i < kMaxLnPer; i++) {
-            const int c = tid + i * kThreads;
-            if (c < C) { const float d = v[i] - mean; sq += d * d; }
-        }
-        const float var = block_sum(sq, red) / (float)C;
-        const float rstd = rsqrtf(var + 1e-5f);
-        const XT* lw = reinterpret_cast<const XT*>(p.ln_w);
-        const XT* lb = reinterpret_cast<const XT*>(p.ln_b);
+        for (int j = 0; j < kLnChunks; j++) {
+            const int c = tid + j * kConsumers;
+            if (c < nch)
 #pragma unroll
-        for (int i = 0; i < kMaxLnPer; i++) {
-            const int c = tid + i * kThreads;
-            if (c < C) {
-                const float n = rstd * (v[i] - mean);
-                const XT o = from_f<XT>(n * to_f<XT>(lw[c]) + to_f<XT>(lb[c]));
-                xsv[c] = o;
-                if (blockIdx.x == 0 && p.ln_out) reinterpret_cast<XT*>(p.ln_out)[c] = o;
+                for (int e = 0; e < E; e++) { const float d = v[j][e] - mean; sq += d * d; }
+        }
+        const float rstd = rsqrtf(consumer_sum(sq, misc) / (float)C + 1e-5f);
+#pragma unroll
+        for (int j = 0; j < kLnChunks; j++) {
+            const int c = tid + j * kConsumers;
+            if (c < nch) {
+                float w[E], b[E], o[E];
+                Vec<XT>::unpack(lw[j], w);
+                Vec<XT>::unpack(lb[j], b);
+#pragma unroll
+                for (int e = 0; e < E; e++) o[e] = (rstd * (v[j][e] - mean)) * w[e] + b[e];
+                const uint4 packed = Vec<XT>::pack(o);
+                reinterpret_cast<uint4*>(xs)[c] = packed;
+                if (blockIdx.x == 0 && p.ln_out) reinterpret_cast<uint4*>(p.ln_out)[c] = packed;
             }
         }
     }
+    consumer_sync();
+    return true;
+}
+
+// LM head: reduce the per-thread best (value, index) over the CTA, publish it,
+// and let the last CTA to finish pick the token and advance the device state.
+__device__ void lmhead_finish(const GemvParams& p, float best_v, int best_i, float* misc) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float* sv = misc;
+    int* si = reinterpret_cast<int*>(misc + kConsumerWarps);
+    __shared__ int s_last;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+        if (ov > best_v || (ov == best_v && oi < best_i)) { best_v = ov; best_i = oi; }
+    }
+    if (lane == 0) { sv[warp] = best_v; si[warp] = best_i; }
+    consumer_sync();
+    if (tid == 0) {
+        float bv = sv[0];
+        int bi = si[0];
+        for (int w = 1; w < kConsumerWarps; w++)
+            if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
+        p.part_val[blockIdx.x] = bv;
+        p.part_idx[blockIdx.x] = bi;
+        __threadfence();
+        const unsigned ticket = atomicAdd(p.counter, 1u);
+        s_last = (ticket == gridDim.x - 1);
+    }
+    consumer_sync();
+    if (!s_last) return;
+    __threadfence();
+    float bv = -FLT_MAX;
+    int bi = 0x7fffffff;
+    for (int b = tid; b < (int)gridDim.x; b += kConsumers) {
+        const float v = __ldcg(&p.part_val[b]);
+        const int i = __ldcg(&p.part_idx[b]);
+        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    consumer_sync();
+    if (lane == 0) { sv[warp] = bv; si[warp] = bi; }
+    consumer_sync();
+    if (tid == 0) {
+        for (int w = 1; w < kConsumerWarps; w++)
+            if (sv[w] > sv[0] || (sv[w] == sv[0] && si[w] < si[0])) { sv[0] = sv[w]; si[0] = si[w]; }
+        *p.counter = 0u;
+        if (p.advance) {
+            const int pos = *p.pos_io;
+            const int next = (pos + 1 < p.n_prompt) ? p.prompt[pos + 1] : si[0];
+            if (p.history) p.history[pos + 1] = next;
+            *p.token_io = next;
+            *p.pos_io = pos + 1;
+        } else if (p.token_io) {
+            *p.token_io = si[0];
+        }
+    }
+}
+
+// Bias / GELU / pre-GELU epilogue of one output row.
+template <typename XT, typename OT>
+__device__ __forceinline__ void store_row(const GemvParams& p, int row, float acc, float bias) {
+    float pre = acc + bias;
+    if (p.pre_gelu) reinterpret_cast<OT*>(p.pre_gelu)[row] = from_f<OT>(pre);
+    const float o = p.do_gelu ? gelu_tanh(pre) : pre;
+    reinterpret_cast<OT*>(p.out)[row] = from_f<OT>(o);
+}
+
+// ---------------------------------------------------------------------------
+// Kernel A: one row tile per CTA (the per-layer matrices).  A producer warp
+// stages the tile (and any further tiles through the ring); the 8 consumer
+// warps split the tile's rows into pairs and, for short tiles, split K.
+// ---------------------------------------------------------------------------
+template <int WK, typename OT, int PRO, int EPI>
+__global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
+    using XT = typename WTraits<WK>::XT;
+    constexpr int kWB = (WK == WK_F32) ? 4 : (WK == WK_BF16 ? 2 : 1);
+    constexpr bool k8 = (WK == WK_I8 || WK == WK_FP8);
+    extern __shared__ __align__(16) unsigned char smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + kMaxStages;
+    uint64_t* aux_bar = empty + kMaxStages;
+    float* red = reinterpret_cast<float*>(smem + kBarBytes);
+    float* misc = red + kRedFloats;  // 16 floats of reduction scratch
+    unsigned char* xs = smem + kSmemHeader;
+    const int x_bytes = ((p.K * (int)sizeof(XT)) + 15) & ~15;
+    unsigned char* aux = xs + x_bytes;
+    unsigned char* stages = aux + p.aux_bytes;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const size_t row_bytes = (size_t)p.K * kWB;
+    const int R = p.rows_per_tile, NS = p.nstages, G = gridDim.x;
+    const int rows_bytes_tile = (int)(((size_t)R * row_bytes + 15) & ~(size_t)15);
+
+    if (tid == 0) {
+        for (int s = 0; s < NS; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        mbar_init(aux_bar, 1);
+        mbar_fence_init();
+    }
     __syncthreads();
 
-    // ---- 4. tiles ----
+    if (warp == kConsumerWarps) {  // producer: weights never depend on other kernels
+        if (lane == 0) {
+            const unsigned char* Wb = reinterpret_cast<const unsigned char*>(p.W);
+            for (int it = 0;; ++it) {
+                const int t = blockIdx.x + it * G;
+                if (t >= p.ntiles) break;
+                const int s = it % NS;
+                if (it >= NS && !mbar_wait(&empty[s], (uint32_t)(((it / NS) - 1) & 1))) break;
+                const int r0 = t * R, nr = min(R, p.M - r0);
+                const uint32_t wbytes = (uint32_t)(nr * row_bytes);
+                const uint32_t sbytes = p.scale_in_tile ? (uint32_t)(((nr + 3) & ~3) * 4) : 0u;
+                unsigned char* st = stages + (size_t)s * p.tile_bytes;
+                mbar_arrive_expect_tx(&full[s], wbytes + sbytes);
+                bulk_g2s(st, Wb + (size_t)r0 * row_bytes, wbytes, &full[s]);
+                if (sbytes) bulk_g2s(st + rows_bytes_tile, p.scale + r0, sbytes, &full[s]);
+            }
+        }
+        return;
+    }
+
+    // consumers: parameters first (bias/scale of a CTA that owns one tile)
+    uint4 lw[kLnChunks], lb[kLnChunks];
+    prefetch_ln_params<WK, PRO>(p, lw, lb);
+    const bool one_tile = (p.ntiles <= G);
+    float bias_reg = 0.0f, scale_reg = 1.0f;
+    if (one_tile) {
+        const int row = blockIdx.x * R + tid;
+        if (tid < R && row < p.M) {
+            if (p.bias) bias_reg = to_f<XT>(reinterpret_cast<const XT*>(p.bias)[row]);
+            if (k8 && !p.scale_in_tile) scale_reg = p.scale[row];
+        }
+    }
+    pdl_wait();
+    pdl_trigger();
+    if (!build_x<WK, PRO>(p, xs, aux, aux_bar, misc, lw, lb)) return;
+
     const int nch = (int)(row_bytes / 16);
     float best_v = -FLT_MAX;
     int best_i = 0x7fffffff;
     int it = 0;
     for (int t = blockIdx.x; t < p.ntiles; t += G, ++it) {
         const int s = it % NS;
-        const uint32_t parity = (uint32_t)((it / NS) & 1);
-        const int r0 = t * R, nr = min(R, p.M - r0);
+        if (!mbar_wait(&full[s], (uint32_t)((it / NS) & 1))) return;
         const unsigned char* tile = stages + (size_t)s * p.tile_bytes;
-        if (!mbar_wait(&bars[s], parity)) return;
-
+        const int r0 = t * R, nr = min(R, p.M - r0);
+        float srow = scale_reg;
+        if (k8 && p.scale_in_tile && tid < nr) srow = reinterpret_cast<const float*>(tile + rows_bytes_tile)[tid];
         const int npairs = (nr + 1) >> 1;
-        const int splits = npairs >= kWarps ? 1 : kWarps / npairs;
-        for (int slot = warp; slot < npairs * splits; slot += kWarps) {
+        const int splits = npairs >= kConsumerWarps ? 1 : kConsumerWarps / npairs;
+        for (int slot = warp; slot < npairs * splits; slot += kConsumerWarps) {
             const int pair = slot / splits, sp = slot % splits;
             const int ra = 2 * pair, rb = min(2 * pair + 1, nr - 1);
             const int cb = (int)((long)sp * nch / splits), ce = (int)((long)(sp + 1) * nch / splits);
@@ -229,95 +501,141 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
                 red[slot * 2 + 1] = a1;
             }
         }
-        __syncthreads();
-        // tile fully consumed: refill this stage with tile t + NS*G
-        if (tid == 0) {
-            const int tn = t + NS * G;
-            if (tn < p.ntiles) {
-                const int rn = tn * R, nrn = min(R, p.M - rn);
-                const uint32_t bytes = (uint32_t)(nrn * row_bytes);
-                mbar_arrive_expect_tx(&bars[s], bytes);
-                bulk_g2s(stages + (size_t)s * p.tile_bytes, Wb + (size_t)rn * row_bytes, bytes, &bars[s]);
-            }
-        }
-        for (int r = tid; r < nr; r += kThreads) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);  // this warp has finished reading the stage
+        consumer_sync();
+        for (int r = tid; r < nr; r += kConsumers) {
             const int pair = r >> 1;
             float acc = 0.0f;
             for (int sp = 0; sp < splits; sp++) acc += red[(pair * splits + sp) * 2 + (r & 1)];
             const int row = r0 + r;
-            if constexpr (WK == WK_I8 || WK == WK_FP8) acc *= p.scale[row];
+            if constexpr (k8) acc *= (one_tile || p.scale_in_tile) ? srow : p.scale[row];
             if constexpr (EPI == EPI_STORE) {
-                float pre = acc;
-                if (p.bias) pre += to_f<XT>(reinterpret_cast<const XT*>(p.bias)[row]);
-                if (p.pre_gelu) reinterpret_cast<OT*>(p.pre_gelu)[row] = from_f<OT>(pre);
-                const float o = p.do_gelu ? gelu_tanh(pre) : pre;
-                reinterpret_cast<OT*>(p.out)[row] = from_f<OT>(o);
+                const float b = p.bias ? (one_tile ? bias_reg : to_f<XT>(reinterpret_cast<const XT*>(p.bias)[row]))
+                                       : 0.0f;
+                store_row<XT, OT>(p, row, acc, b);
             } else {
                 reinterpret_cast<float*>(p.out)[row] = acc;
                 if (row < p.vocab && acc > best_v) { best_v = acc; best_i = row; }
             }
         }
-        __syncthreads();  // red is reused by the next tile
+        consumer_sync();  // red is reused by the next tile
     }
+    if constexpr (EPI == EPI_LMHEAD) lmhead_finish(p, best_v, best_i, misc);
+}
 
-    if constexpr (EPI == EPI_LMHEAD) {
-        // block argmax: largest value, lowest index on ties
-        __shared__ float s_v[kWarps];
-        __shared__ int s_i[kWarps];
-        __shared__ int s_last;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
-            if (ov > best_v || (ov == best_v && oi < best_i)) { best_v = ov; best_i = oi; }
+// One 16-byte weight chunk of one row against x.
+template <int WK>
+__device__ __forceinline__ float chunk_dot1(const uint4& w, const unsigned char* xs, int c) {
+    float a = 0.0f, b = 0.0f;
+    chunk_dot2<WK>(w, w, xs, c, a, b);  // the second row is the same registers; the compiler drops it
+    return a;
+}
+
+// ---------------------------------------------------------------------------
+// Kernel B: streaming (matrices larger than one tile per CTA, e.g. the LM
+// head).  Every warp owns a ring of small row tiles: its lane 0 issues the
+// bulk copies, the warp waits on its own mbarriers, its lanes are split across
+// the tile's rows (32/R lanes per row, short shuffle reductions, two
+// accumulators per lane), it writes its rows and re-arms the stage.  No
+// block-wide barrier in the streaming loop.  Warp tiles are interleaved over
+// all warps of the grid.
+// ---------------------------------------------------------------------------
+template <int WK, typename OT, int PRO, int EPI>
+__global__ void __launch_bounds__(kConsumers) gemv_stream_kernel(const GemvParams p) {
+    using XT = typename WTraits<WK>::XT;
+    constexpr int kWB = (WK == WK_F32) ? 4 : (WK == WK_BF16 ? 2 : 1);
+    constexpr bool k8 = (WK == WK_I8 || WK == WK_FP8);
+    extern __shared__ __align__(16) unsigned char smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [warp][stage]
+    uint64_t* aux_bar = full + kConsumerWarps * kMaxWarpStages;
+    float* misc = reinterpret_cast<float*>(smem + kBarBytes) + kRedFloats;
+    unsigned char* xs = smem + kSmemHeader;
+    const int x_bytes = ((p.K * (int)sizeof(XT)) + 15) & ~15;
+    unsigned char* aux = xs + x_bytes;
+    unsigned char* stages = aux + p.aux_bytes;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const size_t row_bytes = (size_t)p.K * kWB;
+    const int R = p.rows_per_tile, NSW = p.nstages;
+    const int LPR = 32 / R;  // lanes per row (R is a power of two <= 32)
+    const int rows_bytes_tile = (int)(((size_t)R * row_bytes + 15) & ~(size_t)15);
+    const int gw = blockIdx.x * kConsumerWarps + warp, GW = gridDim.x * kConsumerWarps;
+    const int my_tiles = (p.ntiles > gw) ? (p.ntiles - gw + GW - 1) / GW : 0;
+    uint64_t* my_full = full + warp * kMaxWarpStages;
+    unsigned char* my_stages = stages + (size_t)warp * NSW * p.tile_bytes;
+    const unsigned char* Wb = reinterpret_cast<const unsigned char*>(p.W);
+
+    if (tid == 0) {
+        for (int i = 0; i < kConsumerWarps * NSW; i++) mbar_init(&full[(i / NSW) * kMaxWarpStages + i % NSW], 1);
+        mbar_init(aux_bar, 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+
+    auto issue = [&](int k) {  // lane 0: stage warp tile k of this warp
+        const int t = gw + k * GW;
+        const int r0 = t * R, nr = min(R, p.M - r0);
+        const int s = k % NSW;
+        const uint32_t wbytes = (uint32_t)(nr * row_bytes);
+        const uint32_t sbytes = p.scale_in_tile ? (uint32_t)(((nr + 3) & ~3) * 4) : 0u;
+        unsigned char* st = my_stages + (size_t)s * p.tile_bytes;
+        mbar_arrive_expect_tx(&my_full[s], wbytes + sbytes);
+        bulk_g2s(st, Wb + (size_t)r0 * row_bytes, wbytes, &my_full[s]);
+        if (sbytes) bulk_g2s(st + rows_bytes_tile, p.scale + r0, sbytes, &my_full[s]);
+    };
+    if (lane == 0)
+        for (int k = 0; k < NSW && k < my_tiles; k++) issue(k);
+
+    uint4 lw[kLnChunks], lb[kLnChunks];
+    prefetch_ln_params<WK, PRO>(p, lw, lb);
+    pdl_wait();
+    pdl_trigger();
+    if (!build_x<WK, PRO>(p, xs, aux, aux_bar, misc, lw, lb)) return;
+
+    const int nch = (int)(row_bytes / 16);
+    const int rr = lane / LPR, sub = lane % LPR;
+    float best_v = -FLT_MAX;
+    int best_i = 0x7fffffff;
+    for (int k = 0; k < my_tiles; k++) {
+        const int s = k % NSW;
+        if (!mbar_wait(&my_full[s], (uint32_t)((k / NSW) & 1))) return;
+        const unsigned char* tile = my_stages + (size_t)s * p.tile_bytes;
+        const int t = gw + k * GW;
+        const int r0 = t * R, nr = min(R, p.M - r0);
+        float acc0 = 0.0f, acc1 = 0.0f;
+        if (rr < nr) {
+            const unsigned char* wr = tile + (size_t)rr * row_bytes;
+            int c = sub;
+#pragma unroll 2
+            for (; c + LPR < nch; c += 2 * LPR) {
+                const uint4 w0 = *reinterpret_cast<const uint4*>(wr + (size_t)c * 16);
+                const uint4 w1 = *reinterpret_cast<const uint4*>(wr + (size_t)(c + LPR) * 16);
+                acc0 += chunk_dot1<WK>(w0, xs, c);
+                acc1 += chunk_dot1<WK>(w1, xs, c + LPR);
+            }
+            if (c < nch) acc0 += chunk_dot1<WK>(*reinterpret_cast<const uint4*>(wr + (size_t)c * 16), xs, c);
         }
-        if (lane == 0) { s_v[warp] = best_v; s_i[warp] = best_i; }
-        __syncthreads();
-        if (tid == 0) {
-            float bv = s_v[0];
-            int bi = s_i[0];
-            for (int w = 1; w < kWarps; w++)
-                if (s_v[w] > bv || (s_v[w] == bv && s_i[w] < bi)) { bv = s_v[w]; bi = s_i[w]; }
-            p.part_val[blockIdx.x] = bv;
-            p.part_idx[blockIdx.x] = bi;
-            __threadfence();
-            const unsigned ticket = atomicAdd(p.counter, 1u);
-            s_last = (ticket == gridDim.x - 1);
+        float acc = acc0 + acc1;
+        for (int o = LPR / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (sub == 0 && rr < nr) {
+            const int row = r0 + rr;
+            if constexpr (k8)
+                acc *= p.scale_in_tile ? reinterpret_cast<const float*>(tile + rows_bytes_tile)[rr] : p.scale[row];
+            if constexpr (EPI == EPI_STORE) {
+                store_row<XT, OT>(p, row, acc, p.bias ? to_f<XT>(reinterpret_cast<const XT*>(p.bias)[row]) : 0.0f);
+            } else {
+                reinterpret_cast<float*>(p.out)[row] = acc;
+                if (row < p.vocab && acc > best_v) { best_v = acc; best_i = row; }
+            }
         }
-        __syncthreads();
-        if (s_last) {
-            __threadfence();
-            float bv = -FLT_MAX;
-            int bi = 0x7fffffff;
-            for (int b = tid; b < (int)gridDim.x; b += kThreads) {
-                const float v = __ldcg(&p.part_val[b]);
-                const int i = __ldcg(&p.part_idx[b]);
-                if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-            }
-            if (lane == 0) { s_v[warp] = bv; s_i[warp] = bi; }
-            __syncthreads();
-            if (tid == 0) {
-                for (int w = 1; w < kWarps; w++)
-                    if (s_v[w] > s_v[0] || (s_v[w] == s_v[0] && s_i[w] < s_i[0])) { s_v[0] = s_v[w]; s_i[0] = s_i[w]; }
-                *p.counter = 0u;
-                if (p.advance) {
-                    const int pos = *p.pos_io;
-                    const int next = (pos + 1 < p.n_prompt) ? p.prompt[pos + 1] : s_i[0];
-                    if (p.history) p.history[pos + 1] = next;
-                    *p.token_io = next;
-                    *p.pos_io = pos + 1;
-                } else if (p.token_io) {
-                    *p.token_io = s_i[0];
-                }
-            }
+        __syncwarp();
+        if (lane == 0 && k + NSW < my_tiles) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // our reads before the async refill
+            issue(k + NSW);
         }
     }
+    if constexpr (EPI == EPI_LMHEAD) lmhead_finish(p, best_v, best_i, misc);
 }
 
 // ---------------------------------------------------------------------------
@@ -325,39 +643,70 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
 // ---------------------------------------------------------------------------
 size_t gemv_smem_bytes(const GemvParams& p, int wk) {
     const size_t xb = (size_t)p.K * (wk == WK_F32 ? 4 : 2);
-    return 64 + kRedFloats * 4 + ((xb + 15) & ~(size_t)15) + (size_t)p.nstages * p.tile_bytes;
+    const size_t rings = (size_t)(p.stream ? kConsumerWarps : 1) * p.nstages * p.tile_bytes;
+    return kSmemHeader + ((xb + 15) & ~(size_t)15) + (size_t)p.aux_bytes + rings;
 }
+
+// Streaming tuning knobs (read once): GPT2B_GEMV_TILE_KB (warp tile bytes of
+// kernel B), GPT2B_GEMV_STAGE_KB (ring bytes per CTA), GPT2B_GEMV_CTAS_PER_SM.
+static int env_int(const char* name, int dflt) {
+    const char* v = getenv(name);
+    return (v && *v) ? atoi(v) : dflt;
+}
+static const int g_tile_kb = env_int("GPT2B_GEMV_TILE_KB", 12);
+static const int g_stage_kb = env_int("GPT2B_GEMV_STAGE_KB", 200);
+static const int g_ctas_per_sm = env_int("GPT2B_GEMV_CTAS_PER_SM", 1);
 
 bool plan_gemv(GemvParams& p, int wk, int nsm, bool single_wave) {
     const size_t row_bytes = (size_t)p.K * wkind_bytes(wk);
-    const size_t kTileTarget = 32 * 1024, kTileMax = 96 * 1024;
-    if (row_bytes == 0 || row_bytes > kTileMax) return false;
-    int r_stream = (int)(kTileTarget / row_bytes);
-    if (r_stream < 1) r_stream = 1;
-    if (r_stream > kRedFloats - 16) r_stream = kRedFloats - 16;
+    const size_t kOneTileMax = single_wave ? 96 * 1024 : 32 * 1024;
+    if (row_bytes == 0 || row_bytes > 96 * 1024) return false;
+    const bool w8 = (wk == WK_I8 || wk == WK_FP8);
     const int r_even = (p.M + nsm - 1) / nsm;
-    if (r_even <= r_stream || (single_wave && (size_t)r_even * row_bytes <= kTileMax && r_even <= kRedFloats - 16)) {
+    if ((size_t)r_even * row_bytes <= kOneTileMax && r_even <= kRedFloats - 16) {
+        // kernel A: one tile per CTA, the whole matrix in flight at once
+        p.stream = 0;
         p.rows_per_tile = r_even;
         p.ntiles = (p.M + r_even - 1) / r_even;
         p.grid = p.ntiles;
         p.nstages = 1;
+        p.scale_in_tile = (w8 && r_even % 4 == 0 && p.M % 4 == 0 && aligned16(p.scale)) ? 1 : 0;
+        const size_t rows_b = ((size_t)r_even * row_bytes + 15) & ~(size_t)15;
+        p.tile_bytes = (int)((rows_b + (p.scale_in_tile ? (size_t)r_even * 4 : 0) + 15) & ~(size_t)15);
     } else {
-        p.rows_per_tile = r_stream;
-        p.ntiles = (p.M + r_stream - 1) / r_stream;
-        p.grid = std::min(p.ntiles, 2 * nsm);
-        const int per = (p.ntiles + p.grid - 1) / p.grid;
-        p.nstages = std::max(1, std::min(3, per));
+        // kernel B: per-warp rings of R-row tiles, R a power of two <= 32
+        p.stream = 1;
+        int r = 1;
+        while (r < 32 && (size_t)(2 * r) * row_bytes <= (size_t)g_tile_kb * 1024) r *= 2;
+        p.rows_per_tile = r;
+        p.ntiles = (p.M + r - 1) / r;
+        p.scale_in_tile = (w8 && r % 4 == 0 && p.M % 4 == 0 && aligned16(p.scale)) ? 1 : 0;
+        const size_t rows_b = ((size_t)r * row_bytes + 15) & ~(size_t)15;
+        p.tile_bytes = (int)((rows_b + (p.scale_in_tile ? (size_t)r * 4 : 0) + 15) & ~(size_t)15);
+        const int warps_needed = p.ntiles;
+        p.grid = std::max(1, std::min(nsm * std::max(1, g_ctas_per_sm),
+                                      (warps_needed + kConsumerWarps - 1) / kConsumerWarps));
+        const size_t budget = (size_t)g_stage_kb * 1024;
+        p.nstages = (int)std::max<size_t>(1, std::min<size_t>(kMaxWarpStages, budget / ((size_t)kConsumerWarps *
+                                                                                          p.tile_bytes)));
     }
-    p.tile_bytes = (int)(((size_t)p.rows_per_tile * row_bytes + 15) & ~(size_t)15);
+    p.x_vec = aligned16(p.x) ? 1 : 0;
     return true;
 }
 
 template <int WK, typename OT, int PRO, int EPI>
 static cudaError_t launch_one(const GemvParams& p, cudaStream_t s, bool pdl) {
+    const size_t smem = gemv_smem_bytes(p, WK);
+    if ((int)smem > max_dyn_smem() - 1024) return cudaErrorInvalidValue;
+    if (p.stream) {
+        auto k = gemv_stream_kernel<WK, OT, PRO, EPI>;
+        static unsigned long long smem_set = 0;
+        cudaError_t e = ensure_smem_limit(k, &smem_set);
+        if (e != cudaSuccess) return e;
+        return launch_k(k, dim3(p.grid), dim3(kConsumers), smem, s, pdl, p);
+    }
     auto k = gemv_kernel<WK, OT, PRO, EPI>;
     static unsigned long long smem_set = 0;
-    const size_t smem = gemv_smem_bytes(p, WK);
-    if ((int)smem > max_dyn_smem()) return cudaErrorInvalidValue;
     cudaError_t e = ensure_smem_limit(k, &smem_set);
     if (e != cudaSuccess) return e;
     return launch_k(k, dim3(p.grid), dim3(kThreads), smem, s, pdl, p);
@@ -379,12 +728,16 @@ static cudaError_t dispatch_wk(const GemvParams& p, bool out_f32, int pro, int e
         case PRO_PLAIN: return launch_one<WK, XT, PRO_PLAIN, EPI_STORE>(p, s, pdl);
         case PRO_RES_LN: return launch_one<WK, XT, PRO_RES_LN, EPI_STORE>(p, s, pdl);
         case PRO_EMB_LN: return launch_one<WK, XT, PRO_EMB_LN, EPI_STORE>(p, s, pdl);
+        case PRO_ATTN_MERGE: return launch_one<WK, XT, PRO_ATTN_MERGE, EPI_STORE>(p, s, pdl);
     }
     return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_gemv(const GemvParams& p, int wk, bool out_f32, int pro, int epi, cudaStream_t s, bool pdl) {
-    if (pro != PRO_PLAIN && p.K > kMaxLnPer * kThreads) return cudaErrorInvalidValue;
+    const int E = (wk == WK_F32) ? 4 : 8;
+    if ((pro == PRO_RES_LN || pro == PRO_EMB_LN) && (p.K % E != 0 || p.K / E > kLnChunks * kConsumers))
+        return cudaErrorInvalidValue;
+    if (pro == PRO_ATTN_MERGE && p.K != p.attn_heads * 64) return cudaErrorInvalidValue;
     switch (wk) {
         case WK_F32: return dispatch_wk<WK_F32>(p, out_f32, pro, epi, s, pdl);
         case WK_BF16: return dispatch_wk<WK_BF16>(p, out_f32, pro, epi, s, pdl);

@@ -1,4 +1,4 @@
-// internal.h -- host-side interfaces between the library's translation units.
+// internal.h -- interfaces between the library's translation units.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -9,9 +9,10 @@ namespace gpt2b {
 enum WKind { WK_F32 = 0, WK_BF16 = 1, WK_I8 = 2, WK_FP8 = 3 };
 // x-vector source of a GEMV launch
 enum Prologue {
-    PRO_PLAIN = 0,   // x read from memory
-    PRO_RES_LN = 1,  // r = res_in + delta (stored), x = LayerNorm(r)
-    PRO_EMB_LN = 2   // e = wte[token] + wpe[pos] (stored), x = LayerNorm(e)
+    PRO_PLAIN = 0,      // x read from memory
+    PRO_RES_LN = 1,     // r = res_in + delta (stored), x = LayerNorm(r)
+    PRO_EMB_LN = 2,     // e = wte[token] + wpe[pos] (stored), x = LayerNorm(e)
+    PRO_ATTN_MERGE = 3  // x = LSE merge of the attention split partials (stored as atty)
 };
 // output of a GEMV launch
 enum Epilogue {
@@ -20,6 +21,15 @@ enum Epilogue {
 };
 
 inline int wkind_bytes(int wk) { return wk == WK_F32 ? 4 : (wk == WK_BF16 ? 2 : 1); }
+
+// Position chunking of the engine's flash-decoding attention: `splits` CTAs
+// per head, chunks a multiple of 16 positions.  Shared by the attention kernel
+// (which writes the partials) and the GEMV prologue that merges them.
+__host__ __device__ inline int engine_attn_chunk(int total, int splits) {
+    int chunk = (total + splits - 1) / splits;
+    chunk = (chunk + 15) & ~15;
+    return chunk < 16 ? 16 : chunk;
+}
 
 struct GemvParams {
     // the matrix-vector product
@@ -32,6 +42,10 @@ struct GemvParams {
     int M = 0, K = 0, do_gelu = 0;
     // tiling (filled by plan_gemv)
     int rows_per_tile = 0, ntiles = 0, nstages = 1, tile_bytes = 0, grid = 0;
+    int stream = 0;               // 0: one tile per CTA (kernel A); 1: per-warp streaming rings (kernel B)
+    int scale_in_tile = 0;        // 8-bit row scales travel with the weight tile
+    int x_vec = 0;                // x is 16-byte aligned (vector loads)
+    int aux_bytes = 0;            // shared memory for PRO_ATTN_MERGE partials
     // PRO_RES_LN / PRO_EMB_LN
     const void* res_in = nullptr;  // C, activation type
     const void* delta = nullptr;   // C, activation type
@@ -46,6 +60,12 @@ struct GemvParams {
     const float* wte_scale = nullptr;   // Vp
     const void* wpe = nullptr;          // maxT x C
     int vocab = 0, maxT = 0;
+    // PRO_ATTN_MERGE: partials [head][split] (+ [head][split][64] for out)
+    const float* part_out = nullptr;
+    const float* part_max = nullptr;
+    const float* part_lse = nullptr;
+    void* atty_out = nullptr;     // merged attention output (block 0), activation type
+    int attn_heads = 0, attn_splits = 0;
     // EPI_LMHEAD
     float* part_val = nullptr;    // >= grid
     int* part_idx = nullptr;      // >= grid
@@ -62,12 +82,12 @@ struct GemvParams {
 enum KvKind { KV_F32 = 0, KV_BF16 = 1, KV_I8 = 2, KV_FP8 = 3 };
 
 // Decode attention for the engine: fused KV append + flash-decoding over
-// `splits` CTAs per head + last-CTA merge into atty.  kv_layer / kv_scale_layer
-// point at one layer's [K|V] cache and scales; counters (NH) must start at 0.
-cudaError_t launch_attention_engine(int kv, void* atty, const void* qkv, void* kv_layer, float* kv_scale_layer,
-                                    const int* d_pos, int NH, int maxT, int splits, float* part_out,
-                                    float* part_max, float* part_lse, unsigned* counters, cudaStream_t st,
-                                    bool pdl);
+// `splits` CTAs per head; writes the per-split partials (un-normalised out,
+// max, exp-sum) that the following projection GEMV merges (PRO_ATTN_MERGE).
+// kv_layer / kv_scale_layer point at one layer's [K|V] cache and scales.
+cudaError_t launch_attention_engine(int kv, const void* qkv, void* kv_layer, float* kv_scale_layer, const int* d_pos,
+                                    int NH, int maxT, int splits, float* part_out, float* part_max, float* part_lse,
+                                    cudaStream_t st, bool pdl);
 int attn_engine_max_chunk(int kv);  // positions one engine CTA stages at once
 
 // per-translation-unit device error readers
