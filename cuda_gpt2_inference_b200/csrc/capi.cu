@@ -63,7 +63,8 @@ const char* gpt2b_status_string(int s) {
 
 int gpt2b_device_error(int* code) {
     if (!code) return GPT2B_ERR_INVALID_ARG;
-    const int v[4] = {gemv_device_error(), attention_device_error(), norm_device_error(), sampler_device_error()};
+    const int v[5] = {gemv_device_error(), attention_device_error(), norm_device_error(), sampler_device_error(),
+                      persistent_device_error()};
     *code = 0;
     for (int x : v) {
         if (x < 0) return GPT2B_ERR_CUDA;

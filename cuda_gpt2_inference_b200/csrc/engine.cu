@@ -27,8 +27,11 @@
 #include "common.cuh"
 #include "internal.h"
 
+#include <math.h>
 #include <stdio.h>
 #include <string.h>
+
+#include <algorithm>
 #include <string>
 #include <vector>
 
@@ -69,6 +72,11 @@ struct gpt2b_engine {
     int steps_per_graph = 8;
     cudaGraphExec_t graph_multi = nullptr, graph_one = nullptr;
     bool graphs_valid = false;
+    // persistent decode kernel (persistent.cu): its exchange arena and params
+    bool persist_ok = false, use_persistent = false;
+    unsigned char* xchg = nullptr;
+    size_t xchg_bytes = 0;
+    PersistParams pp;
 };
 
 namespace {
@@ -122,6 +130,7 @@ void free_engine(gpt2b_engine* e) {
     if (e->params) cudaFree(e->params);
     if (e->acts) cudaFree(e->acts);
     if (e->kv) cudaFree(e->kv);
+    if (e->xchg) cudaFree(e->xchg);
     if (e->stream) cudaStreamDestroy(e->stream);
     delete e;
 }
@@ -174,6 +183,15 @@ cudaError_t ensure_graphs(gpt2b_engine* e) {
 
 // n forwards from the device-resident token/position.
 cudaError_t run_steps(gpt2b_engine* e, int n) {
+    if (e->use_persistent) {
+        if (n <= 0) return cudaSuccess;
+        cudaError_t err = cudaMemsetAsync(e->pp.abort_flag, 0, sizeof(int), e->stream);
+        if (err != cudaSuccess) return err;
+        PersistParams p = e->pp;
+        p.n_steps = n;
+        p.n_prompt = e->lm_p.n_prompt;
+        return launch_persistent(e->wk, e->kvk, p, e->stream);
+    }
     if (!e->use_graph) {
         for (int i = 0; i < n; i++) {
             cudaError_t err = launch_step(e);
@@ -198,6 +216,66 @@ cudaError_t run_steps(gpt2b_engine* e, int n) {
 
 __global__ void set_history_kernel(int* history, const int* d_token, const int* d_pos) {
     history[*d_pos] = *d_token;
+}
+
+// Plans the persistent decode kernel when the shape allows it: splits per
+// head (as many as fill the SMs, at most 96 positions each), ring stages per
+// warp (as many as fit in shared memory), and the zero-initialised exchange
+// arena: tagged words per layer and phase, per-(layer, head) KV flags, the
+// epoch counter and the abort flag.
+cudaError_t setup_persistent(gpt2b_engine* e, int nsm) {
+    const gpt2b_config& c = e->cfg;
+    const int C = c.channels, NH = c.num_heads, L = c.num_layers, maxT = c.max_seq_len;
+    int coop = 0;
+    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, e->device);
+    const int S = std::min(nsm / NH, persist_max_splits());
+    if (!coop || !persist_supported(C, NH, C / NH, maxT, S, nsm)) return cudaSuccess;
+    int nsw = 0;
+    for (int k = persist_max_stages(); k >= 2 && !nsw; k--) {
+        const int b = persist_smem_bytes(e->wk, e->kvk, C, k);
+        if (b > 0 && b <= max_dyn_smem()) nsw = k;
+    }
+    if (!nsw) return cudaSuccess;
+    const int G = nsm;
+    const size_t n_qkv = (size_t)L * 3 * C, n_c = (size_t)L * C, n_fc = (size_t)L * 4 * C;
+    const size_t n_part = (size_t)L * NH * S * (64 + 2), n_lm = 2 * (size_t)G;
+    const size_t words = n_qkv + 3 * n_c + n_fc + n_part + n_lm;
+    const size_t flags = (size_t)L * NH;
+    size_t bytes = align256(words * 8) + align256(flags * 4) + 256;
+    cudaError_t err = cudaMalloc(&e->xchg, bytes);
+    if (err != cudaSuccess) return err;
+    if ((err = cudaMemset(e->xchg, 0, bytes)) != cudaSuccess) return err;
+    e->xchg_bytes = bytes;
+    PersistParams& p = e->pp;
+    unsigned long long* w = reinterpret_cast<unsigned long long*>(e->xchg);
+    p.ll_qkv = w; w += n_qkv;
+    p.ll_atty = w; w += n_c;
+    p.ll_part = w; w += n_part;
+    p.ll_proj = w; w += n_c;
+    p.ll_fc = w; w += n_fc;
+    p.ll_fcproj = w; w += n_c;
+    p.ll_lm = w;
+    unsigned char* tail = e->xchg + align256(words * 8);
+    p.kv_flag = reinterpret_cast<unsigned*>(tail);
+    tail += align256(flags * 4);
+    p.d_epoch = reinterpret_cast<unsigned*>(tail);
+    p.abort_flag = reinterpret_cast<int*>(tail + 16);
+    p.C = C; p.L = L; p.NH = NH; p.V = c.vocab_size; p.Vp = c.padded_vocab_size; p.maxT = maxT;
+    p.splits = S; p.nsw = nsw; p.G = G;
+    p.attn_scale = 1.0f / sqrtf(64.0f);
+    p.W[0] = e->p[0]; p.W[1] = e->p[4]; p.W[2] = e->p[6]; p.W[3] = e->p[10]; p.W[4] = e->p[12];
+    for (int g = 0; g < 5; g++) p.S[g] = e->sc[g];
+    p.wpe = e->p[1];
+    p.ln1w = e->p[2]; p.ln1b = e->p[3]; p.qkvb = e->p[5]; p.attprojb = e->p[7];
+    p.ln2w = e->p[8]; p.ln2b = e->p[9]; p.fcb = e->p[11]; p.fcprojb = e->p[13];
+    p.lnfw = e->p[14]; p.lnfb = e->p[15];
+    p.kv = e->kv_cache;
+    p.kv_scale = e->kv_scale;
+    p.d_token = e->d_token; p.d_pos = e->d_pos; p.history = e->d_history; p.prompt = e->d_prompt;
+    p.logits = e->logits;
+    e->persist_ok = true;
+    e->use_persistent = true;
+    return cudaSuccess;
 }
 
 int build_engine(const unsigned char* image, size_t nbytes, const float* scales, size_t nscales, int wmode,
@@ -420,6 +498,7 @@ int build_engine(const unsigned char* image, size_t nbytes, const float* scales,
     plan_gemv(lm, wk, nsm, false);
     if (lm.grid > lm_grid_max) return fail(cudaErrorInvalidConfiguration);
     e->lm_p = lm;
+    if ((err = setup_persistent(e, nsm)) != cudaSuccess) return fail(err);
     *out = e;
     return GPT2B_OK;
 }
@@ -524,6 +603,10 @@ int gpt2b_engine_set_option(gpt2b_engine* e, int option, int value) {
             e->steps_per_graph = value;
             e->graphs_valid = false;
             break;
+        case GPT2B_OPT_PERSISTENT:
+            if (value && !e->persist_ok) return GPT2B_ERR_UNSUPPORTED;
+            e->use_persistent = value != 0;
+            break;
         default: return GPT2B_ERR_INVALID_ARG;
     }
     return GPT2B_OK;
@@ -546,7 +629,7 @@ int gpt2b_engine_device_buffers(const gpt2b_engine* e, float** logits, int** tok
 
 int gpt2b_engine_kernels_per_step(const gpt2b_engine* e, int* n) {
     if (!e || !n) return GPT2B_ERR_INVALID_ARG;
-    *n = 5 * e->cfg.num_layers + 1;
+    *n = e->use_persistent ? 0 : 5 * e->cfg.num_layers + 1;
     return GPT2B_OK;
 }
 

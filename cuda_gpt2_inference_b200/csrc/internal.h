@@ -90,11 +90,47 @@ cudaError_t launch_attention_engine(int kv, const void* qkv, void* kv_layer, flo
                                     cudaStream_t st, bool pdl);
 int attn_engine_max_chunk(int kv);  // positions one engine CTA stages at once
 
+// Persistent decode kernel (persistent.cu): every step of a decode call in
+// one cooperative launch of G CTAs (one per SM).
+struct PersistParams {
+    int C = 0, L = 0, NH = 0, V = 0, Vp = 0, maxT = 0, splits = 0, nsw = 0, G = 0;
+    float attn_scale = 0.125f;
+    // parameters: layer-0 bases of the stacked tensors, storage per weight kind
+    const unsigned char* W[5] = {};  // wte, qkvw, attprojw, fcw, fcprojw
+    const float* S[5] = {};          // their per-row scales (8-bit kinds)
+    const void* wpe = nullptr;
+    const void *ln1w = nullptr, *ln1b = nullptr, *qkvb = nullptr, *attprojb = nullptr, *ln2w = nullptr,
+               *ln2b = nullptr, *fcb = nullptr, *fcprojb = nullptr, *lnfw = nullptr, *lnfb = nullptr;
+    // KV cache [layer][K|V][head][maxT][hs] and 8-bit scales [layer][K|V][head][maxT]
+    unsigned char* kv = nullptr;
+    float* kv_scale = nullptr;
+    // exchange words (step tag << 32 | float bits), zero-initialised
+    unsigned long long *ll_qkv = nullptr, *ll_atty = nullptr, *ll_part = nullptr, *ll_proj = nullptr,
+                       *ll_fc = nullptr, *ll_fcproj = nullptr, *ll_lm = nullptr;
+    unsigned* kv_flag = nullptr;  // [layer][head]: last epoch whose KV append is complete
+    // step state (device)
+    int* d_token = nullptr;
+    int* d_pos = nullptr;
+    int* history = nullptr;
+    const int* prompt = nullptr;
+    int n_prompt = 0;
+    unsigned* d_epoch = nullptr;  // advanced by n_steps per call
+    int* abort_flag = nullptr;    // zero at launch
+    float* logits = nullptr;      // Vp floats of the last step
+    int n_steps = 0;
+};
+bool persist_supported(int C, int NH, int hs, int maxT, int splits, int nsm);
+int persist_max_splits();
+int persist_max_stages();
+int persist_smem_bytes(int wk, int kv, int C, int nsw);  // -1: unsupported kinds, or one CTA does not fit an SM
+cudaError_t launch_persistent(int wk, int kv, const PersistParams& P, cudaStream_t st);
+
 // per-translation-unit device error readers
 int gemv_device_error();
 int attention_device_error();
 int norm_device_error();
 int sampler_device_error();
+int persistent_device_error();
 
 // Chooses rows per tile / stages / grid for an M x K matrix of kind wk.
 // Returns false when the shape cannot be tiled (row larger than a tile).

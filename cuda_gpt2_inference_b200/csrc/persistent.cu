@@ -1,0 +1,1061 @@
+// persistent.cu -- the whole greedy decode loop in one cooperative launch.
+//
+// One CTA per SM, resident for all steps of a call.  A decode step is a chain
+// of phases; per layer:
+//   QKV     rows of W_qkv . LN1(residual)              -> qkv words
+//   ATTN    CTA (head h, split s): KV append + flash-decoding over its
+//           position range (rows staged one layer ahead); split 0 of each head
+//           merges the partials of its head (attention_kvcache.cuh:298-318)
+//                                                       -> atty words
+//   PROJ    rows of W_proj . atty                       -> proj words
+//   FC      rows of gelu(W_fc . LN2(residual + proj))   -> fc words
+//   FCPROJ  rows of W_fcproj . fc                       -> fcproj words
+// then LM: logits = wte . LNf(residual) with a per-CTA argmax and an
+// all-gather of the per-CTA (value, index) pairs, so every CTA knows the next
+// token and carries on with the next step: no launch, no host round trip.
+// The arithmetic of each phase is the per-kernel path's (gemv.cu,
+// attention.cu): the same roundings to the activation type at the same points.
+//
+// Exchange between phases uses 64-bit words holding a 32-bit step tag and a
+// 32-bit value, written with one relaxed store: a consumer's poll returns data
+// and readiness in one L2 round trip, with no fence and no grid barrier on the
+// data path.  The residual stream and every LayerNorm are recomputed in each
+// CTA from the exchanged phase outputs, so the residual is never exchanged.
+// Tags are a per-call epoch plus the step, so words of an earlier step or call
+// never match.  A buffer is rewritten only one step later, after every CTA has
+// passed the LM all-gather of the step that read it.  Every poll is bounded; a
+// CTA whose wait runs out records GPT2B_DEVERR_GRID_TIMEOUT and raises an
+// abort flag that makes every other CTA leave at its next poll.  A CTA leaves
+// only when none of its bulk copies is still in flight.
+//
+// Weights: CTA b owns rows [b*M/G, (b+1)*M/G) of every matrix.  A producer
+// warp streams them, in consumption order across phases, layers and steps,
+// through a ring of stages of 16 row-units of C elements (16 rows of K = C, or
+// 8 half-rows of K = 4C), with the rows' bias and scale values in the stage
+// tail; so the ring runs ahead while the consumers wait for their inputs.
+// Consumer warp w takes rows w and w + 8 of a stage (one row for K = 4C), two
+// independent dot products sharing each x chunk and one shuffle reduction.
+//
+// Shapes: head size 64, C <= 1024, heads x splits <= CTAs, at most 96
+// positions per attention CTA (persist_supported); the engine uses the
+// per-kernel path otherwise.
+#include "common.cuh"
+#include "internal.h"
+
+#include <float.h>
+
+namespace gpt2b {
+
+GPT2B_DEFINE_ERROR_READER(persistent_device_error)
+
+namespace {
+
+constexpr int kCW = 8;                // consumer warps
+constexpr int kCT = kCW * 32;         // consumer threads
+constexpr int kThreads = kCT + 32;    // + the producer warp
+constexpr int kStageUnits = 16;       // row-units of C elements per stage
+constexpr int kTailSlot = 96;         // a 16-byte aligned window of 16 bias (or scale) values
+constexpr int kTail = 2 * kTailSlot;  // stage tail: bias window + scale window
+constexpr int kMaxNs = 24;            // ring stages (upper bound)
+constexpr int kKvRows = 96;           // positions per attention CTA
+constexpr int kHSz = 64;              // head size
+constexpr int kMaxSplits = 32;        // attention splits per head
+constexpr int kMiscFloats = 128;      // reduction scratch, new-row codes and scales, stop flag
+constexpr int kGatherJ = 16;          // exchange words per consumer thread and gather (4C <= 4096)
+constexpr uint32_t kPollLimit = 1u << 22;
+enum { kPhQkv = 0, kPhProj = 1, kPhFc = 2, kPhFcproj = 3, kPhLm = 4 };
+
+// Phase timeline for profiling builds (-DGPT2B_PERSIST_TRACE): consumer
+// thread 0 of every CTA stamps %globaltimer at phase boundaries of the first
+// kTraceSteps steps.  Off in the library build.
+#ifdef GPT2B_PERSIST_TRACE
+constexpr int kTraceSteps = 4, kTraceCtas = 160, kTraceEv = 160;
+__device__ unsigned long long g_trace[kTraceSteps * kTraceCtas * kTraceEv];
+#define PTRACE(ev)                                                                            \
+    do {                                                                                      \
+        if (tid == 0 && step < kTraceSteps && (ev) < kTraceEv && b < kTraceCtas) {            \
+            unsigned long long t_;                                                            \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                            \
+            g_trace[((size_t)step * kTraceCtas + b) * kTraceEv + (ev)] = t_;                  \
+        }                                                                                     \
+    } while (0)
+// per-stage stamps of CTA 0: producer issue time, consumer warp 0 wait start / wait end / done
+constexpr int kTraceStages = 2048;
+__device__ unsigned long long g_trace_stage[kTraceStages * 8];
+__device__ __forceinline__ unsigned long long gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+#define PTRACE_STAGE(k, idx)                                                         \
+    do {                                                                             \
+        if (b == 0 && (idx) < kTraceStages) g_trace_stage[(idx) * 8 + (k)] = gtimer(); \
+    } while (0)
+#else
+#define PTRACE(ev) \
+    do {           \
+    } while (0)
+#define PTRACE_STAGE(k, idx) \
+    do {                     \
+    } while (0)
+#endif
+
+// ---------------------------------------------------------------------------
+// exchange words
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void ll_store(unsigned long long* p, float v, uint32_t tag) {
+    const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ll_load(const unsigned long long* p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+__device__ __forceinline__ bool aborted(const PersistParams& P) {
+    return *(volatile const int*)P.abort_flag != 0;
+}
+__device__ __noinline__ void give_up(const PersistParams& P) {
+    report_device_error(GPT2B_DEVERR_GRID_TIMEOUT);
+    atomicExch(P.abort_flag, 1);
+}
+
+// Words i = tid + j*kCT (i < n) of src into out[j]; all loads of a round are
+// in flight together.  False on timeout (recorded) or abort.
+__device__ __noinline__ bool ll_gather(const PersistParams& P, const unsigned long long* src, int n, uint32_t tag,
+                                       float* out) {
+    const int tid = threadIdx.x;
+    uint32_t pending = 0;
+#pragma unroll
+    for (int j = 0; j < kGatherJ; j++)
+        if (tid + j * kCT < n) pending |= 1u << j;
+    for (uint32_t it = 0; pending; ++it) {
+        unsigned long long w[kGatherJ];
+#pragma unroll
+        for (int j = 0; j < kGatherJ; j++)
+            if (pending & (1u << j)) w[j] = ll_load(src + tid + j * kCT);
+#pragma unroll
+        for (int j = 0; j < kGatherJ; j++)
+            if ((pending & (1u << j)) && (uint32_t)(w[j] >> 32) == tag) {
+                out[j] = __uint_as_float((uint32_t)w[j]);
+                pending &= ~(1u << j);
+            }
+        if (!pending) break;
+        if (it > kPollLimit) { give_up(P); return false; }
+        if ((it & 15) == 15 && aborted(P)) return false;
+        __nanosleep(32);
+    }
+    return true;
+}
+
+// consumer-only barriers (named barrier 1, the 256 consumer threads)
+__device__ __forceinline__ void cta_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+__device__ __forceinline__ bool cta_any(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, 1, 256, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v)
+        : "memory");
+    return r != 0;
+}
+__device__ __forceinline__ float cta_sum(float v, float* scratch) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    v = warp_sum(v);
+    if (lane == 0) scratch[w] = v;
+    cta_sync();
+    float t = (lane < kCW) ? scratch[lane] : 0.0f;
+    t = warp_sum(t);
+    cta_sync();
+    return t;
+}
+__device__ __forceinline__ float cta_max(float v, float* scratch) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    v = warp_max(v);
+    if (lane == 0) scratch[w] = v;
+    cta_sync();
+    float t = (lane < kCW) ? scratch[lane] : -FLT_MAX;
+    t = warp_max(t);
+    cta_sync();
+    return t;
+}
+__device__ __forceinline__ void best_merge(float& bv, int& bi, float ov, int oi) {
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// phases
+// ---------------------------------------------------------------------------
+template <int WK> struct PTraits;
+template <> struct PTraits<WK_F32> { using XT = float; static constexpr int kWB = 4; };
+template <> struct PTraits<WK_BF16> { using XT = __nv_bfloat16; static constexpr int kWB = 2; };
+template <> struct PTraits<WK_I8> { using XT = __nv_bfloat16; static constexpr int kWB = 1; };
+template <> struct PTraits<WK_FP8> { using XT = __nv_bfloat16; static constexpr int kWB = 1; };
+
+// Rows, stage geometry and this CTA's row range of phase `ph`: K = C phases
+// take 16 rows per stage, FCPROJ (K = 4C) 8 rows per stage in two K-halves.
+struct PhaseRows {
+    int M, kparts, rs, c0, c1;  // rows, K-parts per row, rows per stage, CTA range
+};
+__device__ __forceinline__ PhaseRows phase_rows(const PersistParams& P, int ph, int b) {
+    PhaseRows r;
+    const int C = P.C;
+    r.M = (ph == kPhQkv) ? 3 * C : (ph == kPhFc) ? 4 * C : (ph == kPhLm) ? P.Vp : C;
+    r.kparts = (ph == kPhFcproj) ? 2 : 1;
+    r.rs = (ph == kPhFcproj) ? kStageUnits / 2 : kStageUnits;
+    r.c0 = b * r.M / P.G;
+    r.c1 = (b + 1) * r.M / P.G;
+    return r;
+}
+__device__ __forceinline__ int phase_widx(int ph) { return ph == kPhLm ? 0 : ph + 1; }
+
+// One 16-byte weight chunk (chunk index c of the x vector) against x in shared memory.
+template <int WK>
+__device__ __forceinline__ float chunk_dot(const uint4& w, const unsigned char* xs, int c) {
+    float a = 0.0f, b = 0.0f;
+    if constexpr (WK == WK_F32) {
+        const float4 x = *reinterpret_cast<const float4*>(xs + (size_t)c * 16);
+        a = fmaf(__uint_as_float(w.x), x.x, a); b = fmaf(__uint_as_float(w.y), x.y, b);
+        a = fmaf(__uint_as_float(w.z), x.z, a); b = fmaf(__uint_as_float(w.w), x.w, b);
+    } else if constexpr (WK == WK_BF16) {
+        const uint4 x = *reinterpret_cast<const uint4*>(xs + (size_t)c * 16);
+        const uint32_t xw[4] = {x.x, x.y, x.z, x.w}, ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            a = fmaf(bf16lo(ww[i]), bf16lo(xw[i]), a);
+            b = fmaf(bf16hi(ww[i]), bf16hi(xw[i]), b);
+        }
+    } else {
+        const uint4 xa = *reinterpret_cast<const uint4*>(xs + (size_t)c * 32);
+        const uint4 xb = *reinterpret_cast<const uint4*>(xs + (size_t)c * 32 + 16);
+        const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float x0 = bf16lo(xw[2 * i]), x1 = bf16hi(xw[2 * i]);
+            const float x2 = bf16lo(xw[2 * i + 1]), x3 = bf16hi(xw[2 * i + 1]);
+            if constexpr (WK == WK_I8) {
+                const uint32_t p = ww[i] ^ 0x80808080u;
+                a = fmaf(i8_to_f(p, 0), x0, a); b = fmaf(i8_to_f(p, 1), x1, b);
+                a = fmaf(i8_to_f(p, 2), x2, a); b = fmaf(i8_to_f(p, 3), x3, b);
+            } else {
+                a = fmaf(e4m3_to_f(ww[i], 0), x0, a); b = fmaf(e4m3_to_f(ww[i], 1), x1, b);
+                a = fmaf(e4m3_to_f(ww[i], 2), x2, a); b = fmaf(e4m3_to_f(ww[i], 3), x3, b);
+            }
+        }
+    }
+    return a + b;
+}
+
+// Two rows' 16-byte chunks against the same x chunk (loaded once).
+template <int WK>
+__device__ __forceinline__ void chunk_dot2(const uint4& w0, const uint4& w1, const unsigned char* xs, int c, float& a0,
+                                           float& a1) {
+    if constexpr (WK == WK_F32) {
+        const float4 x = *reinterpret_cast<const float4*>(xs + (size_t)c * 16);
+        a0 = fmaf(__uint_as_float(w0.x), x.x, a0); a1 = fmaf(__uint_as_float(w1.x), x.x, a1);
+        a0 = fmaf(__uint_as_float(w0.y), x.y, a0); a1 = fmaf(__uint_as_float(w1.y), x.y, a1);
+        a0 = fmaf(__uint_as_float(w0.z), x.z, a0); a1 = fmaf(__uint_as_float(w1.z), x.z, a1);
+        a0 = fmaf(__uint_as_float(w0.w), x.w, a0); a1 = fmaf(__uint_as_float(w1.w), x.w, a1);
+    } else if constexpr (WK == WK_BF16) {
+        const uint4 x = *reinterpret_cast<const uint4*>(xs + (size_t)c * 16);
+        const uint32_t xw[4] = {x.x, x.y, x.z, x.w}, u0[4] = {w0.x, w0.y, w0.z, w0.w}, u1[4] = {w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float xl = bf16lo(xw[i]), xh = bf16hi(xw[i]);
+            a0 = fmaf(bf16lo(u0[i]), xl, a0); a1 = fmaf(bf16lo(u1[i]), xl, a1);
+            a0 = fmaf(bf16hi(u0[i]), xh, a0); a1 = fmaf(bf16hi(u1[i]), xh, a1);
+        }
+    } else {
+        const uint4 xa = *reinterpret_cast<const uint4*>(xs + (size_t)c * 32);
+        const uint4 xb = *reinterpret_cast<const uint4*>(xs + (size_t)c * 32 + 16);
+        const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+        const uint32_t u0[4] = {w0.x, w0.y, w0.z, w0.w}, u1[4] = {w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float x[4] = {bf16lo(xw[2 * i]), bf16hi(xw[2 * i]), bf16lo(xw[2 * i + 1]), bf16hi(xw[2 * i + 1])};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                if constexpr (WK == WK_I8) {
+                    a0 = fmaf(i8_to_f(u0[i] ^ 0x80808080u, j), x[j], a0);
+                    a1 = fmaf(i8_to_f(u1[i] ^ 0x80808080u, j), x[j], a1);
+                } else {
+                    a0 = fmaf(e4m3_to_f(u0[i], j), x[j], a0);
+                    a1 = fmaf(e4m3_to_f(u1[i], j), x[j], a1);
+                }
+            }
+        }
+    }
+}
+
+template <int KV>
+__device__ __forceinline__ float kv_code(uint32_t word, int j) {
+    if constexpr (KV == KV_FP8) return e4m3_to_f(word, j);
+    else return (float)(int8_t)((word >> (8 * j)) & 0xffu);
+}
+// 8-bit KV code of x at row scale `scale` (the per-kernel KV write's expression).
+template <int KV>
+__device__ __forceinline__ uint8_t kv_encode(float x, float scale) {
+    if constexpr (KV == KV_FP8) {
+        return (uint8_t)__nv_cvt_float_to_fp8(x / scale, __NV_SATFINITE, __NV_E4M3);
+    } else {
+        int q = __float2int_rn(x / scale);
+        q = q < -127 ? -127 : (q > 127 ? 127 : q);
+        return (uint8_t)(int8_t)q;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// shared memory layout
+// ---------------------------------------------------------------------------
+struct PSmem {
+    int stage_bytes, ring, kvbuf, uni, res, misc, bars, total;
+};
+
+template <int WK, int KV>
+__host__ __device__ inline PSmem persist_layout(int C, int ns) {
+    const int xb = (WK == WK_F32) ? 4 : 2;
+    const int wb = PTraits<WK>::kWB;
+    const int kvb = (KV == KV_F32) ? 4 : (KV == KV_BF16 ? 2 : 1);
+    const bool k8 = (KV == KV_I8 || KV == KV_FP8);
+    const int rpp = kCT / (kHSz * kvb / 16);
+    PSmem s;
+    s.stage_bytes = kStageUnits * C * wb + kTail;
+    int off = 0;
+    s.ring = off; off += ns * s.stage_bytes;
+    s.kvbuf = off; off += 2 * kKvRows * kHSz * kvb + (k8 ? 2 * (kKvRows + 8) * 4 : 0);
+    off = (off + 15) & ~15;
+    s.uni = off;  // x vector of the current phase, or the attention scratch
+    const int xs_bytes = 4 * C * xb;
+    const int attn_bytes = (rpp * kHSz + 3 * kHSz + kKvRows + (kMaxSplits - 1) * (kHSz + 2)) * 4;
+    off += ((xs_bytes > attn_bytes ? xs_bytes : attn_bytes) + 15) & ~15;
+    s.res = off; off += C * 4;
+    s.misc = off; off += kMiscFloats * 4;
+    s.bars = off; off += (2 * kMaxNs + 2) * 8;
+    s.total = off;
+    return s;
+}
+
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
+template <int WK, int KV>
+__global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const PersistParams P) {
+    using XT = typename PTraits<WK>::XT;
+    constexpr int kWB = PTraits<WK>::kWB;
+    constexpr int kXB = (int)sizeof(XT);
+    constexpr bool w8 = (WK == WK_I8 || WK == WK_FP8);
+    constexpr bool k8 = (KV == KV_I8 || KV == KV_FP8);
+    constexpr int kvb = (KV == KV_F32) ? 4 : (KV == KV_BF16 ? 2 : 1);
+    constexpr int kRowB = kHSz * kvb;  // bytes of one K or V row
+    constexpr int kLP = kRowB / 16;    // lanes per row in the attention loops
+    constexpr int kRPP = kCT / kLP;    // rows per pass
+    constexpr int kE = 16 / kvb;       // elements per 16-byte slice
+    using KT = typename PTraits<(KV == KV_F32) ? WK_F32 : WK_BF16>::XT;  // KV element type (float kinds)
+    extern __shared__ __align__(16) unsigned char sm[];
+    const PSmem lay = persist_layout<WK, KV>(P.C, P.nsw);
+    unsigned char* ring = sm + lay.ring;
+    unsigned char* kvbuf = sm + lay.kvbuf;
+    unsigned char* xs = sm + lay.uni;
+    float* res = reinterpret_cast<float*>(sm + lay.res);
+    float* misc = reinterpret_cast<float*>(sm + lay.misc);
+    int* misc_i = reinterpret_cast<int*>(misc);
+    volatile int* stop = misc_i + (kMiscFloats - 1);  // consumers left early: the producer stops
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + lay.bars);
+    uint64_t* empty = full + kMaxNs;
+    uint64_t* kv_bar = empty + kMaxNs;
+    // attention scratch (aliases xs: never live at the same time)
+    float* accbuf = reinterpret_cast<float*>(xs);
+    float* q_s = accbuf + kRPP * kHSz;
+    float* kcur = q_s + kHSz;
+    float* vcur = kcur + kHSz;
+    float* p_s = vcur + kHSz;
+    float* mrg = p_s + kKvRows;  // (splits - 1) x (64 + 2) partials of the head
+    uint8_t* cur8 = reinterpret_cast<uint8_t*>(misc + 64);  // 8-bit codes of the new K | V rows
+    float* cur_sc = misc + 96;                              // and their scales
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int C = P.C, L = P.L, NH = P.NH, maxT = P.maxT, S = P.splits, G = P.G, NS = P.nsw;
+    const int b = blockIdx.x;
+    const int unit_bytes = C * kWB;  // one row-unit: a row of K = C, half a K-half of K = 4C
+    const uint32_t epoch0 = *P.d_epoch;
+    const int pos0 = *P.d_pos;
+    int tok = *P.d_token;
+    // the same checks in every CTA, so all of them leave together
+    if (pos0 < 0 || pos0 + P.n_steps > maxT) {
+        if (b == 0 && tid == 0) report_device_error(GPT2B_DEVERR_BAD_POS);
+        return;
+    }
+    if (tok < 0 || tok >= P.V) {
+        if (b == 0 && tid == 0) report_device_error(GPT2B_DEVERR_BAD_TOKEN);
+        return;
+    }
+    if (tid == 0) {
+        for (int i = 0; i < NS; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kCW);
+        }
+        mbar_init(kv_bar, 1);
+        *stop = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();  // the last block-wide barrier: producer and consumers part here
+
+    // =====================================================================
+    // producer warp: every weight stage of every phase, layer and step
+    // =====================================================================
+    if (warp == kCW) {
+        if (lane != 0) return;
+        int issued = 0, st = 0;
+        for (int step = 0; step < P.n_steps; step++) {
+            for (int u = 0; u <= 4 * L; u++) {
+                const int l = (u == 4 * L) ? 0 : (u >> 2);
+                const int ph = (u == 4 * L) ? kPhLm : (u & 3);
+                const PhaseRows pr = phase_rows(P, ph, b);
+                const int widx = phase_widx(ph);
+                const int part_bytes = (kStageUnits / pr.rs) * unit_bytes;  // per row and stage
+                const size_t row_bytes = (size_t)pr.kparts * part_bytes;
+                const unsigned char* wl = P.W[widx] + (size_t)l * pr.M * row_bytes;
+                const unsigned char* bias = nullptr;
+                if (ph == kPhQkv) bias = reinterpret_cast<const unsigned char*>(P.qkvb);
+                else if (ph == kPhProj) bias = reinterpret_cast<const unsigned char*>(P.attprojb);
+                else if (ph == kPhFc) bias = reinterpret_cast<const unsigned char*>(P.fcb);
+                else if (ph == kPhFcproj) bias = reinterpret_cast<const unsigned char*>(P.fcprojb);
+                if (bias) bias += (size_t)l * pr.M * kXB;
+                const float* scl = w8 ? P.S[widx] + (ph == kPhLm ? 0 : (size_t)l * pr.M) : nullptr;
+                for (int r0 = pr.c0; r0 < pr.c1; r0 += pr.rs) {
+                    const int nr = min(pr.rs, pr.c1 - r0);
+                    for (int kq = 0; kq < pr.kparts; kq++) {
+                        if (issued >= NS) {  // wait until all consumer warps released this stage
+                            const uint32_t par = (uint32_t)(((issued / NS) - 1) & 1);
+                            bool ok = false;
+                            for (uint32_t i = 0; i < kMbarSpinLimit; ++i) {
+                                if (mbar_try_wait(&empty[st], par)) { ok = true; break; }
+                                if (*stop) break;
+                            }
+                            if (!ok) goto producer_drain;
+                        }
+                        unsigned char* sd = ring + (size_t)st * lay.stage_bytes;
+                        unsigned char* tail = sd + kStageUnits * unit_bytes;
+                        const bool last = (kq == pr.kparts - 1);
+                        uint32_t bb = 0, sb = 0;
+                        size_t ba = 0, sa = 0;
+                        if (last && bias) {
+                            ba = ((size_t)r0 * kXB) & ~(size_t)15;
+                            bb = (uint32_t)((((size_t)(r0 + nr) * kXB + 15) & ~(size_t)15) - ba);
+                        }
+                        if (last && w8) {
+                            sa = ((size_t)r0 * 4) & ~(size_t)15;
+                            sb = (uint32_t)((((size_t)(r0 + nr) * 4 + 15) & ~(size_t)15) - sa);
+                        }
+                        PTRACE_STAGE(0, issued);
+                        mbar_arrive_expect_tx(&full[st], (uint32_t)(nr * part_bytes) + bb + sb);
+                        if (pr.kparts == 1) {
+                            bulk_g2s(sd, wl + (size_t)r0 * row_bytes, (uint32_t)(nr * part_bytes), &full[st]);
+                        } else {
+                            for (int i = 0; i < nr; i++)
+                                bulk_g2s(sd + (size_t)i * part_bytes,
+                                         wl + (size_t)(r0 + i) * row_bytes + (size_t)kq * part_bytes,
+                                         (uint32_t)part_bytes, &full[st]);
+                        }
+                        if (bb) bulk_g2s(tail, bias + ba, bb, &full[st]);
+                        if (sb)
+                            bulk_g2s(tail + kTailSlot, reinterpret_cast<const unsigned char*>(scl) + sa, sb, &full[st]);
+                        issued++;
+                        if (++st == NS) st = 0;
+                    }
+                }
+            }
+        }
+    producer_drain:
+        // leave with none of this warp's copies in flight
+        for (int k = issued > NS ? issued - NS : 0; k < issued; k++)
+            mbar_wait(&full[k % NS], (uint32_t)((k / NS) & 1));
+        return;
+    }
+
+    // =====================================================================
+    // consumers (256 threads)
+    // =====================================================================
+    const bool attn_cta = b < NH * S;
+    const int ah = attn_cta ? b / S : 0, as = attn_cta ? b % S : 0;
+    const size_t NHmT = (size_t)NH * maxT;
+    bool bad = false;
+    int cst = 0;            // ring position of the next stage
+    uint32_t cpar = 0;      // and its full-barrier parity
+    int kv_issued = 0, kv_uses = 0;
+#ifdef GPT2B_PERSIST_TRACE
+    int consumed_n = 0;
+#endif
+
+    // ---- KV staging of an attention CTA: one buffer; the next layer's rows
+    //      are staged as soon as this layer's attention is done ----
+    auto kv_issue = [&](int step, int l) {  // tid 0 only
+        const int pos = pos0 + step, total = pos + 1;
+        const int chunk = engine_attn_chunk(total, S);
+        const int j0 = as * chunk, j1 = min(j0 + chunk, total);
+        if (j1 <= j0) return;
+        if (step > 0) {
+            // rows below pos were appended during earlier steps of this call:
+            // acquire the release of step - 1, whose tag is epoch0 + step (rows
+            // written by earlier launches are ordered by the kernel boundary)
+            const uint32_t need = epoch0 + (uint32_t)step;
+            const unsigned* flag = P.kv_flag + l * NH + ah;
+            for (uint32_t it = 0;; ++it) {
+                unsigned f;
+                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(f) : "l"(flag) : "memory");
+                if ((int)(f - need) >= 0) break;
+                if (it > kPollLimit) { give_up(P); bad = true; return; }
+                if ((it & 15) == 15 && aborted(P)) { bad = true; return; }
+                __nanosleep(64);
+            }
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+        }
+        const size_t lk = (size_t)l * 2 * NHmT;  // layer offset in rows
+        const size_t krow = (size_t)ah * maxT + j0;
+        const int n = j1 - j0;
+        const uint32_t rb = (uint32_t)(n * kRowB);
+        uint32_t tx = 2 * rb, sb = 0;
+        size_t k0 = 0;
+        if constexpr (k8) {  // scale copies start at the 16-byte boundary below the first row
+            k0 = krow & ~(size_t)3;
+            sb = (uint32_t)((((krow + n + 3) & ~(size_t)3) - k0) * 4);
+            tx += 2 * sb;
+        }
+        mbar_arrive_expect_tx(kv_bar, tx);
+        bulk_g2s(kvbuf, P.kv + (lk + krow) * kRowB, rb, kv_bar);
+        bulk_g2s(kvbuf + kKvRows * kRowB, P.kv + (lk + NHmT + krow) * kRowB, rb, kv_bar);
+        if constexpr (k8) {
+            const float* sc = P.kv_scale + lk;
+            bulk_g2s(kvbuf + 2 * kKvRows * kRowB, sc + k0, sb, kv_bar);
+            bulk_g2s(kvbuf + 2 * kKvRows * kRowB + (kKvRows + 8) * 4, sc + NHmT + k0, sb, kv_bar);
+        }
+        kv_issued++;
+    };
+    if (attn_cta && tid == 0) kv_issue(0, 0);
+    if (cta_any(bad)) goto consumer_abort;
+
+    {
+        const XT* wpe = reinterpret_cast<const XT*>(P.wpe);
+        float gv[kGatherJ];
+        for (int step = 0; step < P.n_steps; step++) {
+            const uint32_t tag = epoch0 + (uint32_t)step + 1u;
+            const int pos = pos0 + step;
+            PTRACE(kTraceEv - 1);
+            float best_v = -FLT_MAX;
+            int best_i = 0x7fffffff;
+#pragma unroll 1
+            for (int u = 0; u <= 4 * L; u++) {
+                const bool lm = (u == 4 * L);
+                const int l = lm ? 0 : (u >> 2);
+                const int ph = lm ? kPhLm : (u & 3);
+                XT* xv = reinterpret_cast<XT*>(xs);
+
+                // ---------- x of this phase ----------
+                if (ph == kPhQkv || ph == kPhFc || lm) {
+                    // residual update (fcproj of the previous layer, or proj), then LayerNorm
+                    const void* lnw = lm ? P.lnfw : (ph == kPhQkv ? P.ln1w : P.ln2w);
+                    const void* lnb = lm ? P.lnfb : (ph == kPhQkv ? P.ln1b : P.ln2b);
+                    const size_t lo = lm ? 0 : (size_t)l * C;
+                    float lw[4], lb[4];  // parameters loaded before the wait
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const int c = tid + j * kCT;
+                        lw[j] = c < C ? to_f<XT>(reinterpret_cast<const XT*>(lnw)[lo + c]) : 0.0f;
+                        lb[j] = c < C ? to_f<XT>(reinterpret_cast<const XT*>(lnb)[lo + c]) : 0.0f;
+                    }
+                    if (u == 0) {  // embedding: res = round(wte[tok] + wpe[pos]) (encoder_forward_kv)
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            const int c = tid + j * kCT;
+                            if (c < C) {
+                                float e;
+                                if constexpr (w8) {
+                                    const uint8_t code = P.W[0][(size_t)tok * C + c];
+                                    const float v = (WK == WK_I8) ? (float)(int8_t)code : e4m3_to_f((uint32_t)code, 0);
+                                    e = round_to<__nv_bfloat16>(v * P.S[0][tok]);
+                                } else {
+                                    e = to_f<XT>(reinterpret_cast<const XT*>(P.W[0])[(size_t)tok * C + c]);
+                                }
+                                res[c] = round_to<XT>(e + to_f<XT>(wpe[(size_t)pos * C + c]));
+                            }
+                        }
+                    } else {
+                        const unsigned long long* src =
+                            (ph == kPhFc) ? P.ll_proj + (size_t)l * C : P.ll_fcproj + (size_t)(lm ? L - 1 : l - 1) * C;
+                        const bool ok = ll_gather(P, src, C, tag, gv);
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            const int c = tid + j * kCT;
+                            if (c < C) res[c] = round_to<XT>(res[c] + gv[j]);
+                        }
+                        if (cta_any(!ok)) goto consumer_abort;
+                    }
+                    // LayerNorm (layernorm.cuh:171-241): two passes over the rounded
+                    // residual; warp totals in misc[0..7] then misc[8..15], one barrier each
+                    float s = 0.0f;
+#pragma unroll
+                    for (int j = 0; j < 4; j++) if (tid + j * kCT < C) s += res[tid + j * kCT];
+                    s = warp_sum(s);
+                    if (lane == 0) misc[warp] = s;
+                    cta_sync();
+                    s = 0.0f;
+#pragma unroll
+                    for (int w = 0; w < kCW; w++) s += misc[w];
+                    const float mean = s / (float)C;
+                    float q = 0.0f;
+#pragma unroll
+                    for (int j = 0; j < 4; j++)
+                        if (tid + j * kCT < C) { const float d = res[tid + j * kCT] - mean; q += d * d; }
+                    q = warp_sum(q);
+                    if (lane == 0) misc[kCW + warp] = q;
+                    cta_sync();
+                    q = 0.0f;
+#pragma unroll
+                    for (int w = 0; w < kCW; w++) q += misc[kCW + w];
+                    const float rstd = rsqrtf(q / (float)C + 1e-5f);
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const int c = tid + j * kCT;
+                        if (c < C) xv[c] = from_f<XT>((rstd * (res[c] - mean)) * lw[j] + lb[j]);
+                    }
+                } else {
+                    // PROJ: x = atty of this layer; FCPROJ: x = gelu(fc) of this layer
+                    const int n = (ph == kPhProj) ? C : 4 * C;
+                    const unsigned long long* src =
+                        (ph == kPhProj) ? P.ll_atty + (size_t)l * C : P.ll_fc + (size_t)l * 4 * C;
+                    const bool ok = ll_gather(P, src, n, tag, gv);
+#pragma unroll
+                    for (int j = 0; j < kGatherJ; j++)
+                        if (tid + j * kCT < n) xv[tid + j * kCT] = from_f<XT>(gv[j]);
+                    if (cta_any(!ok)) goto consumer_abort;
+                }
+                cta_sync();
+                PTRACE(u * 3 + 0);
+
+                // ---------- the matrix rows of this CTA ----------
+                {
+                    const PhaseRows pr = phase_rows(P, ph, b);
+                    unsigned long long* out = nullptr;
+                    if (ph == kPhQkv) out = P.ll_qkv + (size_t)l * pr.M;
+                    else if (ph == kPhProj) out = P.ll_proj + (size_t)l * pr.M;
+                    else if (ph == kPhFc) out = P.ll_fc + (size_t)l * pr.M;
+                    else if (ph == kPhFcproj) out = P.ll_fcproj + (size_t)l * pr.M;
+                    const bool has_bias = !lm;
+                    const int part_bytes = (kStageUnits / pr.rs) * unit_bytes;
+                    const int pc = part_bytes / 16;                   // chunks per row and stage
+                    const bool two = (pr.rs == kStageUnits);         // rows warp and warp + 8
+                    for (int r0 = pr.c0; r0 < pr.c1; r0 += pr.rs) {
+                        const int nr = min(pr.rs, pr.c1 - r0);
+                        const bool hA = warp < nr, hB = two && warp + kCW < nr;
+                        float k0 = 0.0f, k1 = 0.0f;
+                        for (int kq = 0; kq < pr.kparts; kq++) {
+#ifdef GPT2B_PERSIST_TRACE
+                            if (tid == 0) PTRACE_STAGE(1, consumed_n);
+#endif
+                            if (!mbar_wait(&full[cst], cpar)) bad = true;
+#ifdef GPT2B_PERSIST_TRACE
+                            if (tid == 0) PTRACE_STAGE(2, consumed_n);
+#endif
+                            const unsigned char* sd = ring + (size_t)cst * lay.stage_bytes;
+                            if (hA) {
+                                const unsigned char* wa = sd + (size_t)warp * part_bytes;
+                                const unsigned char* wb2 = sd + (size_t)(warp + kCW) * part_bytes;
+                                float a0 = 0.0f, a1 = 0.0f;
+                                if (hB) {
+                                    for (int c = lane; c < pc; c += 32)
+                                        chunk_dot2<WK>(*reinterpret_cast<const uint4*>(wa + (size_t)c * 16),
+                                                       *reinterpret_cast<const uint4*>(wb2 + (size_t)c * 16), xs,
+                                                       kq * pc + c, a0, a1);
+                                } else {
+                                    for (int c = lane; c < pc; c += 32)
+                                        a0 += chunk_dot<WK>(*reinterpret_cast<const uint4*>(wa + (size_t)c * 16), xs,
+                                                            kq * pc + c);
+                                }
+#ifdef GPT2B_PERSIST_TRACE
+                                if (tid == 0) PTRACE_STAGE(4, consumed_n);
+#endif
+#pragma unroll
+                                for (int o = 16; o > 0; o >>= 1) {
+                                    a0 += __shfl_xor_sync(0xffffffffu, a0, o);
+                                    a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+                                }
+                                k0 += a0;
+                                k1 += a1;
+#ifdef GPT2B_PERSIST_TRACE
+                                if (tid == 0) PTRACE_STAGE(5, consumed_n);
+#endif
+                                // every lane holds both sums: lane 0 emits row A, lane 1 row B
+                                if (kq == pr.kparts - 1 && (lane == 0 || (lane == 1 && hB))) {
+                                    const unsigned char* tail = sd + kStageUnits * unit_bytes;
+                                    const XT* bw = reinterpret_cast<const XT*>(tail + ((r0 * kXB) & 15));
+                                    const float* sw = reinterpret_cast<const float*>(tail + kTailSlot + ((r0 * 4) & 15));
+                                    const int rl = warp + lane * kCW, row = r0 + rl;
+                                    float v = lane ? k1 : k0;
+                                    if constexpr (w8) v *= sw[rl];
+                                    if (has_bias) v += to_f<XT>(bw[rl]);
+                                    if (lm) {
+                                        P.logits[row] = v;
+                                        if (row < P.V) best_merge(best_v, best_i, v, row);
+                                    } else {
+                                        ll_store(out + row, round_to<XT>(ph == kPhFc ? gelu_tanh(v) : v), tag);
+                                    }
+                                }
+                            }
+                            __syncwarp();
+#ifdef GPT2B_PERSIST_TRACE
+                            if (tid == 0) PTRACE_STAGE(3, consumed_n);
+                            consumed_n++;
+#endif
+                            if (lane == 0) mbar_arrive(&empty[cst]);
+                            if (++cst == NS) { cst = 0; cpar ^= 1u; }
+                        }
+                    }
+                }
+                if (cta_any(bad)) goto consumer_abort;
+                PTRACE(u * 3 + 1);
+
+                // ---------- after QKV: attention (head ah, split as) ----------
+                if (ph == kPhQkv && attn_cta) {
+                    const unsigned long long* qkv_w = P.ll_qkv + (size_t)l * 3 * C;
+                    const int total = pos + 1;
+                    const int chunk = engine_attn_chunk(total, S);
+                    const int j0 = as * chunk, j1 = min(j0 + chunk, total);
+                    const int n_local = j1 - j0;
+                    const int s_eff = min(S, (total + chunk - 1) / chunk);
+                    if (tid < 3 * kHSz) {
+                        const unsigned long long* src = qkv_w + (size_t)(tid >> 6) * C + (size_t)ah * kHSz + (tid & 63);
+                        float v = 0.0f;
+                        for (uint32_t it = 0;; ++it) {
+                            const unsigned long long w = ll_load(src);
+                            if ((uint32_t)(w >> 32) == tag) { v = __uint_as_float((uint32_t)w); break; }
+                            if (it > kPollLimit) { give_up(P); bad = true; break; }
+                            if ((it & 15) == 15 && aborted(P)) { bad = true; break; }
+                            __nanosleep(32);
+                        }
+                        (tid < kHSz ? q_s : (tid < 2 * kHSz ? kcur : vcur))[tid & 63] = v;
+                    }
+                    if (cta_any(bad)) goto consumer_abort;
+                    const bool owns = (pos >= j0 && pos < j1);
+                    const size_t lk = (size_t)l * 2 * NHmT;
+                    const size_t krow = (size_t)ah * maxT + pos;
+                    if (owns) {
+                        // append this token's K/V (kv_cache_write_kernel(_w8))
+                        if constexpr (k8) {
+                            if (tid < 64) {
+                                const int which = tid >> 5;
+                                const float* src = which ? vcur : kcur;
+                                const float v0 = src[lane], v1 = src[lane + 32];
+                                const float mx = warp_max(fmaxf(fabsf(v0), fabsf(v1)));
+                                const float sc = mx / (KV == KV_FP8 ? 448.0f : 127.0f);
+                                const uint8_t c0 = sc > 0.0f ? kv_encode<KV>(v0, sc) : (uint8_t)0;
+                                const uint8_t c1 = sc > 0.0f ? kv_encode<KV>(v1, sc) : (uint8_t)0;
+                                uint8_t* dst = P.kv + (lk + (which ? NHmT : 0) + krow) * kRowB;
+                                dst[lane] = c0;
+                                dst[lane + 32] = c1;
+                                cur8[which * 64 + lane] = c0;
+                                cur8[which * 64 + lane + 32] = c1;
+                                if (lane == 0) {
+                                    P.kv_scale[lk + (which ? NHmT : 0) + krow] = sc;
+                                    cur_sc[which] = sc;
+                                }
+                            }
+                        } else {
+                            if (tid < 2 * kHSz) {
+                                const int which = tid >> 6, d = tid & 63;
+                                KT* dst = reinterpret_cast<KT*>(P.kv + (lk + (which ? NHmT : 0) + krow) * kRowB);
+                                dst[d] = from_f<KT>((which ? vcur : kcur)[d]);
+                            }
+                        }
+                        __threadfence();
+                        cta_sync();
+                        // release this step's tag (a max: the flag never goes back)
+                        if (tid == 0)
+                            asm volatile("red.release.gpu.global.max.u32 [%0], %1;" ::"l"(P.kv_flag + l * NH + ah),
+                                         "r"(tag)
+                                         : "memory");
+                    }
+                    float m_run = -FLT_MAX, l_run = 0.0f;
+                    float acc[kE];
+#pragma unroll
+                    for (int e = 0; e < kE; e++) acc[e] = 0.0f;
+                    const int lp = tid % kLP, rg = tid / kLP;
+                    if (n_local > 0) {
+                        if (!mbar_wait(kv_bar, (uint32_t)(kv_uses & 1))) bad = true;
+                        kv_uses++;
+                        const int soff = (int)(((size_t)ah * maxT + j0) & 3);
+                        float* ksc = reinterpret_cast<float*>(kvbuf + 2 * kKvRows * kRowB) + soff;
+                        float* vsc = ksc + (kKvRows + 8);
+                        if (owns) {  // the staged copy holds the stale row of pos: patch it
+                            const int r = pos - j0;
+                            if constexpr (k8) {
+                                if (tid < 128) kvbuf[(tid >> 6) * kKvRows * kRowB + r * kRowB + (tid & 63)] = cur8[tid];
+                                if (tid == 0) { ksc[r] = cur_sc[0]; vsc[r] = cur_sc[1]; }
+                            } else {
+                                if (tid < 2 * kHSz) {
+                                    const int which = tid >> 6, d = tid & 63;
+                                    reinterpret_cast<KT*>(kvbuf + which * kKvRows * kRowB + r * kRowB)[d] =
+                                        from_f<KT>((which ? vcur : kcur)[d]);
+                                }
+                            }
+                        }
+                        if (cta_any(bad)) goto consumer_abort;
+                        const unsigned char* Kst = kvbuf;
+                        const unsigned char* Vst = kvbuf + kKvRows * kRowB;
+                        // scores (the per-kernel engine attention's arithmetic)
+                        for (int rbase = 0; rbase < n_local; rbase += kRPP) {
+                            const int r = rbase + rg;
+                            const bool valid = r < n_local;
+                            const uint4 w = valid ? *reinterpret_cast<const uint4*>(Kst + r * kRowB + lp * 16)
+                                                  : make_uint4(0u, 0u, 0u, 0u);
+                            const float* q = q_s + lp * kE;
+                            float d = 0.0f;
+                            if constexpr (KV == KV_F32) {
+                                d = __uint_as_float(w.x) * q[0] + __uint_as_float(w.y) * q[1] +
+                                    __uint_as_float(w.z) * q[2] + __uint_as_float(w.w) * q[3];
+                            } else if constexpr (KV == KV_BF16) {
+                                const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                                for (int i = 0; i < 4; i++) d += bf16lo(ww[i]) * q[2 * i] + bf16hi(ww[i]) * q[2 * i + 1];
+                            } else {
+                                const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                                for (int i = 0; i < 4; i++)
+#pragma unroll
+                                    for (int j = 0; j < 4; j++) d += kv_code<KV>(ww[i], j) * q[4 * i + j];
+                            }
+#pragma unroll
+                            for (int o = kLP / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+                            if (lp == 0 && valid) {
+                                if constexpr (k8) d *= ksc[r];
+                                p_s[r] = d * P.attn_scale;
+                            }
+                        }
+                        cta_sync();
+                        // one chunk: the online-softmax state starts at (-FLT_MAX, 0)
+                        m_run = cta_max(tid < n_local ? p_s[tid] : -FLT_MAX, misc);
+                        float ev = 0.0f;
+                        if (tid < n_local) { ev = __expf(p_s[tid] - m_run); p_s[tid] = ev; }
+                        l_run = cta_sum(ev, misc);  // ends with a barrier: p_s is complete
+                        for (int r = rg; r < n_local; r += kRPP) {
+                            const uint4 w = *reinterpret_cast<const uint4*>(Vst + r * kRowB + lp * 16);
+                            const float p = p_s[r];
+                            if constexpr (KV == KV_F32) {
+                                acc[0] += p * __uint_as_float(w.x); acc[1] += p * __uint_as_float(w.y);
+                                acc[2] += p * __uint_as_float(w.z); acc[3] += p * __uint_as_float(w.w);
+                            } else if constexpr (KV == KV_BF16) {
+                                const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                                for (int i = 0; i < 4; i++) {
+                                    acc[2 * i] += p * bf16lo(ww[i]);
+                                    acc[2 * i + 1] += p * bf16hi(ww[i]);
+                                }
+                            } else {
+                                const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+                                const float pv = p * vsc[r];
+#pragma unroll
+                                for (int i = 0; i < 4; i++)
+#pragma unroll
+                                    for (int j = 0; j < 4; j++) acc[4 * i + j] += pv * kv_code<KV>(ww[i], j);
+                            }
+                        }
+                    }
+                    cta_sync();  // staged rows and p_s consumed
+                    if (tid == 0) {
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // after the patch writes
+                        if (l + 1 < L) kv_issue(step, l + 1);
+                        else if (step + 1 < P.n_steps) kv_issue(step + 1, 0);
+                    }
+#pragma unroll
+                    for (int e = 0; e < kE; e++) accbuf[rg * kHSz + lp * kE + e] = acc[e];
+                    cta_sync();
+                    float o = 0.0f;
+                    if (tid < kHSz)
+                        for (int g = 0; g < kRPP; g++) o += accbuf[g * kHSz + tid];
+                    PTRACE(u * 3 + 2);
+                    unsigned long long* part = P.ll_part + ((size_t)l * NH + ah) * S * (kHSz + 2);
+                    if (as > 0) {
+                        if (n_local > 0) {  // partial (un-normalised out, max, exp-sum) for split 0
+                            unsigned long long* dst = part + (size_t)as * (kHSz + 2);
+                            if (tid < kHSz) ll_store(dst + tid, o, tag);
+                            if (tid == kHSz) ll_store(dst + kHSz, m_run, tag);
+                            if (tid == kHSz + 1) ll_store(dst + kHSz + 1, l_run, tag);
+                        }
+                    } else {
+                        // split 0 merges the head's partials and publishes atty
+                        const int nw = (s_eff - 1) * (kHSz + 2);  // <= 31 * 66 <= 8 * kCT
+                        if (!ll_gather(P, part + (kHSz + 2), nw, tag, gv)) bad = true;
+#pragma unroll
+                        for (int j = 0; j < 8; j++)
+                            if (tid + j * kCT < nw) mrg[tid + j * kCT] = gv[j];
+                        if (cta_any(bad)) goto consumer_abort;
+                        if (tid < kHSz) {
+                            float mg = m_run;
+                            for (int k = 0; k < s_eff - 1; k++) mg = fmaxf(mg, mrg[k * (kHSz + 2) + kHSz]);
+                            const float r0 = __expf(m_run - mg);
+                            float of = 0.0f + r0 * o, lf = 0.0f + r0 * l_run;
+                            for (int k = 0; k < s_eff - 1; k++) {
+                                const float rs = __expf(mrg[k * (kHSz + 2) + kHSz] - mg);
+                                of += rs * mrg[k * (kHSz + 2) + tid];
+                                lf += rs * mrg[k * (kHSz + 2) + kHSz + 1];
+                            }
+                            ll_store(P.ll_atty + (size_t)l * C + (size_t)ah * kHSz + tid, round_to<XT>(of / lf), tag);
+                        }
+                    }
+                    if (cta_any(bad)) goto consumer_abort;  // also carries a failed kv_issue
+                }
+            }
+
+            // ---------- greedy pick: per-CTA best, all-gather, next token ----------
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {  // lanes 0 and 1 hold candidates
+                const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+                best_merge(best_v, best_i, ov, oi);
+            }
+            if (lane == 0) { misc[warp] = best_v; misc_i[16 + warp] = best_i; }
+            cta_sync();
+            if (tid == 0) {
+                float bv = misc[0];
+                int bi = misc_i[16];
+                for (int w = 1; w < kCW; w++) best_merge(bv, bi, misc[w], misc_i[16 + w]);
+                ll_store(P.ll_lm + 2 * b, bv, tag);
+                ll_store(P.ll_lm + 2 * b + 1, __int_as_float(bi), tag);
+            }
+            {
+                const bool ok = ll_gather(P, P.ll_lm, 2 * G, tag, gv);
+                float* gvals = reinterpret_cast<float*>(xs);
+                int* gidx = reinterpret_cast<int*>(xs) + G;
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    const int wi = tid + j * kCT;
+                    if (wi < 2 * G) {
+                        if (wi & 1) gidx[wi >> 1] = __float_as_int(gv[j]);
+                        else gvals[wi >> 1] = gv[j];
+                    }
+                }
+                if (cta_any(!ok)) goto consumer_abort;
+                PTRACE(4 * L * 3 + 2);
+                float bv = -FLT_MAX;
+                int bi = 0x7fffffff;
+                for (int k = tid; k < G; k += kCT) best_merge(bv, bi, gvals[k], gidx[k]);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                    best_merge(bv, bi, ov, oi);
+                }
+                if (lane == 0) { misc[32 + warp] = bv; misc_i[48 + warp] = bi; }
+                cta_sync();
+                bv = misc[32];
+                bi = misc_i[48];
+                for (int w = 1; w < kCW; w++) best_merge(bv, bi, misc[32 + w], misc_i[48 + w]);
+                // teacher-forced prompt positions, as in the LM-head GEMV epilogue
+                const int next = (pos + 1 < P.n_prompt) ? P.prompt[pos + 1] : bi;
+                if (next < 0 || next >= P.V) {  // no finite logit: every CTA sees the same pick and leaves
+                    if (b == 0 && tid == 0) report_device_error(GPT2B_DEVERR_BAD_TOKEN);
+                    goto consumer_abort;
+                }
+                if (b == 0 && tid == 0) {
+                    P.history[pos + 1] = next;
+                    if (step + 1 == P.n_steps) {
+                        *P.d_token = next;
+                        *P.d_pos = pos + 1;
+                        *P.d_epoch = epoch0 + (uint32_t)P.n_steps;
+                    }
+                }
+                tok = next;
+                cta_sync();  // misc and xs are reused by the next step
+            }
+        }
+    }
+    goto consumer_exit;
+
+consumer_abort:
+    if (tid == 0) *stop = 1;  // the producer stops issuing and drains
+consumer_exit:
+    if (tid == 0 && kv_issued > kv_uses) mbar_wait(kv_bar, (uint32_t)(kv_uses & 1));
+}
+
+// smem_out != null: report the shared memory of a launch with P.C, P.nsw and
+// whether one CTA of it fits on an SM (-1 if not); no launch.
+template <int WK, int KV>
+cudaError_t launch_persist_t(const PersistParams& P, cudaStream_t st, int* smem_out) {
+    auto k = decode_persistent_kernel<WK, KV>;
+    static unsigned long long smem_set = 0;
+    const PSmem lay = persist_layout<WK, KV>(P.C, P.nsw);
+    cudaError_t e = ensure_smem_limit(k, &smem_set);
+    if (e != cudaSuccess) return e;
+    if (smem_out) {
+        int nb = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k, kThreads, lay.total);
+        *smem_out = (e == cudaSuccess && nb >= 1) ? lay.total : -1;
+        return e;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(P.G);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = lay.total;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs co-resident: they wait on one another
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k, P);
+}
+
+cudaError_t persist_dispatch(int wk, int kv, const PersistParams& P, cudaStream_t st, int* smem_out) {
+#define GPT2B_PK(W_, K_) \
+    if (wk == W_ && kv == K_) return launch_persist_t<W_, K_>(P, st, smem_out);
+    GPT2B_PK(WK_F32, KV_F32)
+    GPT2B_PK(WK_BF16, KV_BF16)
+    GPT2B_PK(WK_I8, KV_BF16)
+    GPT2B_PK(WK_I8, KV_I8)
+    GPT2B_PK(WK_FP8, KV_BF16)
+    GPT2B_PK(WK_FP8, KV_FP8)
+#undef GPT2B_PK
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+#ifdef GPT2B_PERSIST_TRACE
+extern "C" int gpt2b_persist_trace(unsigned long long* host, int* steps, int* ctas, int* events) {
+    *steps = kTraceSteps; *ctas = kTraceCtas; *events = kTraceEv;
+    return (int)cudaMemcpyFromSymbol(host, g_trace, sizeof(g_trace));
+}
+extern "C" int gpt2b_persist_trace_stages(unsigned long long* host) {
+    return (int)cudaMemcpyFromSymbol(host, g_trace_stage, sizeof(g_trace_stage));
+}
+#endif
+
+int persist_smem_bytes(int wk, int kv, int C, int nsw) {
+    PersistParams P;
+    P.C = C;
+    P.nsw = nsw;
+    int s = -1;
+    if (persist_dispatch(wk, kv, P, nullptr, &s) != cudaSuccess) return -1;
+    return s;
+}
+
+bool persist_supported(int C, int NH, int hs, int maxT, int splits, int nsm) {
+    if (hs != kHSz || C > 1024 || C % 64 != 0 || (NH * maxT) % 4 != 0) return false;
+    if (splits < 1 || splits > kMaxSplits || NH * splits > nsm) return false;
+    return engine_attn_chunk(maxT, splits) <= kKvRows;
+}
+
+int persist_max_splits() { return kMaxSplits; }
+int persist_max_stages() { return kMaxNs; }
+
+cudaError_t launch_persistent(int wk, int kv, const PersistParams& P, cudaStream_t st) {
+    return persist_dispatch(wk, kv, P, st, nullptr);
+}
+
+}  // namespace gpt2b

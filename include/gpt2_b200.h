@@ -50,7 +50,8 @@ enum {
     GPT2B_DEVERR_MBAR_TIMEOUT = 1, /* a bulk copy never completed within its bound */
     GPT2B_DEVERR_BAD_TOKEN = 2,    /* token id outside [0, vocab) */
     GPT2B_DEVERR_BAD_POS = 3,      /* position outside [0, maxT) */
-    GPT2B_DEVERR_PEER_TIMEOUT = 4  /* a cross-GPU flag wait hit its bound */
+    GPT2B_DEVERR_PEER_TIMEOUT = 4, /* a cross-GPU flag wait hit its bound */
+    GPT2B_DEVERR_GRID_TIMEOUT = 5  /* a wait on another CTA of the persistent decode kernel hit its bound */
 };
 
 const char* gpt2b_status_string(int status);
@@ -251,7 +252,9 @@ enum {
     GPT2B_OPT_USE_GRAPH = 1,  /* 1 (default): replay the captured step graph; 0: launch kernels */
     GPT2B_OPT_USE_PDL = 2,    /* 1 (default): programmatic dependent launch between kernels */
     GPT2B_OPT_SPLITS = 3,     /* attention splits per head for long contexts (default: fills the SMs) */
-    GPT2B_OPT_STEPS_PER_GRAPH = 4 /* decode steps captured into one graph (default 8) */
+    GPT2B_OPT_STEPS_PER_GRAPH = 4, /* decode steps captured into one graph (default 8) */
+    GPT2B_OPT_PERSISTENT = 5  /* 1 (default where the shape allows): the whole decode loop runs in one
+                                 cooperative kernel; 0: per-kernel steps (GEMV / attention launches) */
 };
 
 /* GPT2Config field order (Inference_gpt2/gpt2_model.h:28-35). */
@@ -312,7 +315,9 @@ int gpt2b_engine_set_position(gpt2b_engine* e, int token, int pos);
 /* Waits for the engine stream and copies history[first .. first+count) (the
  * token at each position; history[p+1] is the pick after position p) to host. */
 int gpt2b_engine_history(gpt2b_engine* e, int* out_host, int first, int count);
-/* Kernel launches one step issues (for launch accounting). */
+/* Kernel launches one step issues (for launch accounting); 0 when the
+ * persistent kernel runs: it issues one launch per decode/generate call for
+ * all of that call's steps. */
 int gpt2b_engine_kernels_per_step(const gpt2b_engine* e, int* n);
 
 #ifdef __cplusplus

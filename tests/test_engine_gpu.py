@@ -9,6 +9,8 @@
   compiled from source (oracle/_ref/libref_engine_*.so), teacher-forced.
 * Launch modes (CUDA graph / eager, PDL on/off, device-resident decode) give
   bit-identical results.
+* Both step implementations run every parity case: the persistent decode
+  kernel (one cooperative launch per call) and the per-kernel path.
 """
 from __future__ import annotations
 
@@ -23,6 +25,16 @@ pytestmark = pytest.mark.gpu
 
 MODES = [("f32", "floatx"), ("bf16", "floatx"), ("int8", "floatx"), ("int8", "8bit"), ("fp8", "8bit"),
          ("fp8", "floatx")]
+PATHS = ["persistent", "kernels"]
+
+
+def _engine(img, wmode, kvmode="floatx", sc=None, path="persistent"):
+    """An engine on the requested step implementation (fails if it is unavailable)."""
+    from cuda_gpt2_inference_b200 import OPT_PERSISTENT
+    from cuda_gpt2_inference_b200.engine import Engine
+    eng = Engine.from_buffer(img, wmode, kvmode, sc)
+    eng.set_option(OPT_PERSISTENT, 1 if path == "persistent" else 0)
+    return eng
 
 
 def _quantize(gpt2b, img16: bytes, fmt: str):
@@ -52,12 +64,12 @@ def mini(gpt2b, cuda):
     return cfg, _images(gpt2b, cfg, 31, "test")
 
 
+@pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("wmode,kvmode", MODES)
-def test_mini_model_matches_oracle(mini, orc, wmode, kvmode):
-    from cuda_gpt2_inference_b200.engine import Engine
+def test_mini_model_matches_oracle(mini, orc, wmode, kvmode, path):
     cfg, imgs = mini
     img, sc = imgs[wmode]
-    eng = Engine.from_buffer(img, wmode, kvmode, sc)
+    eng = _engine(img, wmode, kvmode, sc, path)
     prompt = [5, 17, 123, 499, 0]
     n_gen = cfg["maxT"] - len(prompt)
     toks, lg = eng.generate(prompt, n_gen, want_logits=True)
@@ -80,13 +92,12 @@ def test_mini_model_matches_oracle(mini, orc, wmode, kvmode):
 
 def test_launch_modes_bit_identical(mini):
     from cuda_gpt2_inference_b200 import OPT_STEPS_PER_GRAPH, OPT_USE_GRAPH, OPT_USE_PDL
-    from cuda_gpt2_inference_b200.engine import Engine
     cfg, imgs = mini
     img, _ = imgs["bf16"]
     prompt = [1, 2, 3]
     results = []
     for graph, pdl, spg in ((1, 1, 8), (0, 1, 8), (1, 0, 8), (0, 0, 1), (1, 1, 3)):
-        eng = Engine.from_buffer(img, "bf16")
+        eng = _engine(img, "bf16", path="kernels")
         eng.set_option(OPT_USE_GRAPH, graph)
         eng.set_option(OPT_USE_PDL, pdl)
         eng.set_option(OPT_STEPS_PER_GRAPH, spg)
@@ -99,10 +110,67 @@ def test_launch_modes_bit_identical(mini):
         assert np.array_equal(toks, results[0][0]) and np.array_equal(lg, results[0][1])
 
 
-def test_engine_rejects_bad_inputs(mini, gpt2b):
-    from cuda_gpt2_inference_b200.engine import Engine
+@pytest.mark.parametrize("wmode,kvmode", [("bf16", "floatx"), ("int8", "8bit"), ("f32", "floatx")])
+def test_persistent_launch_splits_bit_identical(mini, wmode, kvmode):
+    """One launch for the whole call, one launch per step, and a decode split
+    over several calls give the same tokens (and the same last logits)."""
     cfg, imgs = mini
-    eng = Engine.from_buffer(imgs["bf16"][0], "bf16")
+    img, sc = imgs[wmode]
+    prompt = [7, 8, 9, 10]
+    eng = _engine(img, wmode, kvmode, sc)
+    per_step, lg = eng.generate(prompt, 50, want_logits=True)   # one launch per step
+    one_launch, _ = eng.generate(prompt, 50)                    # one launch in total
+    assert np.array_equal(per_step, one_launch)
+    # the prompt teacher-forced in one call, then 50 steps in calls of 1, 7, 19, 23
+    eng.generate(prompt, 0)
+    for n in (1, 7, 19, 23):
+        eng.decode(n)
+    hist = eng.history(len(prompt), 51)
+    assert np.array_equal(hist, one_launch), (hist[:12], one_launch[:12])
+    eng.close()
+
+
+def test_persistent_matches_kernel_path(mini):
+    """The two step implementations agree to rounding: teacher-forced on the
+    kernel path's tokens, logits cosine >= 0.9999 in BF16."""
+    cfg, imgs = mini
+    img, _ = imgs["bf16"]
+    prompt = [3, 1, 4, 1, 5]
+    ek = _engine(img, "bf16", path="kernels")
+    toks, lk = ek.generate(prompt, 40, want_logits=True)
+    ek.close()
+    ep = _engine(img, "bf16", path="persistent")
+    seq = list(prompt) + list(toks[:-1])
+    _, lp = ep.generate(seq, 0, want_logits=True)
+    ep.close()
+    cos = [cosine(lk[i], lp[i]) for i in range(len(seq))]
+    assert min(cos) >= 0.9999, min(cos)
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("path", PATHS)
+@pytest.mark.parametrize("wmode,kvmode", [("bf16", "floatx"), ("int8", "8bit"), ("fp8", "8bit")])
+def test_long_context_matches_oracle(gpt2b, orc, cuda, wmode, kvmode, path):
+    """Twelve heads over the full 1024-position context: every attention split
+    (up to 96 positions per CTA on the persistent path) and the merge of all of
+    them, teacher-forced against the oracle."""
+    from cuda_gpt2_inference_b200 import weights
+    cfg = weights.mini_config(L=1, NH=12, maxT=1024, V=500, Vp=512)
+    imgs = _images(gpt2b, cfg, 77, "test")
+    img, sc = imgs[wmode]
+    eng = _engine(img, wmode, kvmode, sc, path)
+    prompt = [11, 22, 33]
+    toks, lg = eng.generate(prompt, cfg["maxT"] - len(prompt), want_logits=True)
+    eng.close()
+    m = orc.Model(img, wmode, kvmode, sc)
+    seq = list(prompt) + list(toks[:-1])
+    cos = [cosine(lg[pos], m.step(int(t), pos)) for pos, t in enumerate(seq)]
+    assert min(cos) >= 0.999, (min(cos), int(np.argmin(cos)))
+
+
+def test_engine_rejects_bad_inputs(mini, gpt2b):
+    cfg, imgs = mini
+    eng = _engine(imgs["bf16"][0], "bf16")
     with pytest.raises(gpt2b.Gpt2bError):
         eng.forward(cfg["V"], 0)  # token out of range
     with pytest.raises(gpt2b.Gpt2bError):
@@ -122,13 +190,13 @@ def m124(gpt2b, cuda):
 
 
 @pytest.mark.slow
-def test_124m_fp32_greedy_128_steps(m124, orc):
-    from cuda_gpt2_inference_b200.engine import Engine
+@pytest.mark.parametrize("path", PATHS)
+def test_124m_fp32_greedy_128_steps(m124, orc, path):
     cfg, imgs = m124
     img, _ = imgs["f32"]
     rng = np.random.default_rng(24)
     prompt = rng.integers(0, cfg["V"], 24).astype(np.int32)
-    eng = Engine.from_buffer(img, "f32")
+    eng = _engine(img, "f32", path=path)
     toks, lg = eng.generate(prompt, 128, want_logits=True)
     eng.close()
     m = orc.Model(img, "f32")
@@ -149,10 +217,10 @@ def _ref_engine(orc, name, path):
 
 
 @pytest.mark.slow
+@pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("wmode,kvmode,refname", [("bf16", "floatx", "bf16"), ("int8", "8bit", "int8kv8"),
                                                   ("fp8", "8bit", "fp8kv8")])
-def test_124m_against_reference_engine(m124, orc, tmp_path, wmode, kvmode, refname):
-    from cuda_gpt2_inference_b200.engine import Engine
+def test_124m_against_reference_engine(m124, orc, tmp_path, wmode, kvmode, refname, path):
     cfg, imgs = m124
     img, sc = imgs[wmode]
     path = tmp_path / "model.bin"
@@ -163,7 +231,7 @@ def test_124m_against_reference_engine(m124, orc, tmp_path, wmode, kvmode, refna
     rng = np.random.default_rng(5)
     prompt = rng.integers(0, cfg["V"], 24).astype(np.int32)
     n_gen = 176  # crosses the reference's 150-position switch to split+merge
-    eng = Engine.from_buffer(img, wmode, kvmode, sc)
+    eng = _engine(img, wmode, kvmode, sc, path)
     toks, lg = eng.generate(prompt, n_gen, want_logits=True)
     eng.close()
     seq = list(prompt) + list(toks[:-1])
