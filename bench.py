@@ -412,6 +412,26 @@ def reference_cuda_engine(img, sc, wmode, kvmode):
             "what": "reference inference_gpt2_opt graph loop compiled for sm_100a, wall ms / 999 tokens"}
 
 
+def run_profile_case(args):
+    """Three engine launches: 24-token prefill, decode to position 500, then
+    decode(8) -- the launch a profiler captures (-k <kernel> -s 2 -c 1 on the
+    persistent path)."""
+    import cuda_gpt2_inference_b200 as pkg
+    from cuda_gpt2_inference_b200.engine import Engine
+    wmode, kvmode = CONFIGS[args.config]
+    cfg, _, img, sc = make_model(wmode, kvmode)
+    eng = Engine.from_buffer(img, wmode, kvmode, sc)
+    if args.path == "kernels":
+        eng.set_option(pkg.OPT_PERSISTENT, 0)
+    prompt = np.random.default_rng(24).integers(0, cfg["V"], PROMPT_LEN).astype(np.int32)
+    eng.generate(prompt, 0)
+    eng.decode(500 - PROMPT_LEN)
+    eng.decode(8)
+    print("profile case done:", eng.history(500, 9)[:4].tolist())
+    eng.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -422,8 +442,13 @@ def main():
     ap.add_argument("--path", choices=["persistent", "kernels"], default="persistent",
                     help="decode step implementation (persistent falls back to kernels where unsupported)")
     ap.add_argument("--quick", action="store_true", help="skip the optional extras (GEMV table, CPU and reference bars)")
+    ap.add_argument("--profile-case", action="store_true",
+                    help="small case for profilers: prefill, decode to position 500, then one 8-step decode "
+                         "(the 3rd engine launch); prints no bench line")
     args = ap.parse_args()
     rank, local_rank, world = env_rank()
+    if args.profile_case:
+        return run_profile_case(args)
     if args.impl == "reference":
         return run_reference(args, rank, world)
     return run_ours(args, rank, local_rank, world)
