@@ -41,6 +41,9 @@ CONFIGS = {
     "f32": ("f32", "floatx"),
 }
 METRIC = "ms/token GPT-2 124M b=1 decode (FP32/BF16/INT8/FP8); GEMV GB/s vs HBM peak"
+# GPT-2-XL INT8 weights, BF16 KV, tensor parallel over the launched ranks (TP = N)
+XL_CONFIG = "xl-int8"
+XL_METRIC = "ms/token GPT-2-XL INT8 b=1 decode, tensor parallel over N GPUs"
 
 
 def env_rank():
@@ -412,6 +415,124 @@ def reference_cuda_engine(img, sc, wmode, kvmode):
             "what": "reference inference_gpt2_opt graph loop compiled for sm_100a, wall ms / 999 tokens"}
 
 
+def xl_model(rank, world):
+    """GPT-2-XL INT8 image + scales (random init, spec), generated once by rank 0
+    into /dev/shm and read by every rank."""
+    import torch.distributed as dist
+
+    from cuda_gpt2_inference_b200 import check, lib, weights
+    cfg = weights.GPT2_XL
+    base = "/dev/shm/gpt2b_xl_int8_s1234"
+    if rank == 0 and not os.path.exists(base + ".ok"):
+        img16 = weights.image_stream(cfg, 1234, "spec", "bf16")
+        ob, ns = ctypes.c_size_t(), ctypes.c_size_t()
+        check(lib().gpt2b_quantized_size(img16, len(img16), ctypes.byref(ob), ctypes.byref(ns)))
+        out = ctypes.create_string_buffer(ob.value)
+        sc = np.zeros(ns.value, np.float32)
+        check(lib().gpt2b_quantize_buffer(img16, len(img16), out, sc.ctypes.data_as(ctypes.c_void_p), 0))
+        del img16
+        with open(base + ".bin", "wb") as f:
+            f.write(out.raw)
+        sc.tofile(base + "_scales.bin")
+        open(base + ".ok", "w").close()
+    if world > 1:
+        dist.barrier()
+    with open(base + ".bin", "rb") as f:
+        img = f.read()
+    return cfg, img, np.fromfile(base + "_scales.bin", dtype=np.float32)
+
+
+def run_xl_tp(args, rank, local_rank, world):
+    """GPT-2-XL INT8 (BF16 KV), batch 1, 1000 greedy steps after a 24-token
+    prompt, tensor parallel over the WORLD_SIZE ranks (one engine per GPU,
+    NCCL all-reduces of the row-parallel projections)."""
+    import torch
+    import torch.distributed as dist
+
+    from cuda_gpt2_inference_b200 import tp
+    from cuda_gpt2_inference_b200.engine import Engine
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
+                                device_id=torch.device("cuda", local_rank))
+    cfg, img, sc = xl_model(rank, world)
+    if world > 1:
+        eng = tp.engine(img, "int8", "floatx", sc, rank, world, tp.shared_group_id(rank))
+    else:
+        eng = Engine.from_buffer(img, "int8", "floatx", sc)
+    del img
+    kps = eng.kernels_per_step()
+    prompt = np.random.default_rng(24).integers(0, cfg["V"], PROMPT_LEN).astype(np.int32)
+    first, _ = eng.generate(prompt, 0)
+    g0 = int(first[0])
+    stream = torch.cuda.ExternalStream(eng.stream)
+
+    def step():
+        eng.set_position(g0, PROMPT_LEN)
+        eng.decode(GEN)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        step()
+    end.record(stream)
+    end.synchronize()
+    clk = clocks.stop()
+    t = torch.tensor([start.elapsed_time(end)], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    value = max_ms / (args.steps * GEN)
+    decoded = eng.history(PROMPT_LEN, GEN + 1)
+    e2e_tokens, _ = eng.generate(prompt, GEN)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        eng.generate(prompt, GEN)
+    te = torch.tensor([(time.perf_counter() - t0) * 1e3], device="cuda")
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = float(te.item()) / (args.steps * GEN)
+    peak, peak_kind = measured_peaks()
+    abytes = algo_bytes_per_token(cfg, "int8", "floatx")
+    achieved = abytes / world / (value * 1e-3) / 1e9  # per GPU: each rank reads ~1/TP of the bytes
+    line = {
+        "metric": XL_METRIC, "value": round(value, 5), "unit": "ms/token", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(max_ms / args.steps, 3), "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "gpt2-xl b=1 greedy decode, int8 weights, bf16 kv, 1000 steps after a 24-token "
+                               "prompt (positions 24..1023)",
+                   "model": "gpt2-xl (random init)", "global_batch": 1, "seq_len": cfg["maxT"],
+                   "parallelism": f"tp{world}", "l2": "inputs larger than L2 (~1.7 GB per token)"},
+        "e2e": {"value": round(e2e_value, 5), "unit": "ms/token", "h2d_bytes_per_step": PROMPT_LEN * 4 + 12,
+                "d2h_bytes_per_step": (GEN + 1) * 4},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                     "kernel": "whole decode step per rank (%d kernels + %d NCCL collectives)" % (
+                         kps, 2 * cfg["L"] + 1 if world > 1 else 0),
+                     "algorithmic_bytes_per_token": int(abytes)},
+        "gpu_launches": kps * GEN * args.steps,
+        "clocks": clk,
+        "deterministic": bool(np.array_equal(decoded, e2e_tokens)),
+    }
+    eng.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line))
+    return 0
+
+
 def run_profile_case(args):
     """Three engine launches: 24-token prefill, decode to position 500, then
     decode(8) -- the launch a profiler captures (-k <kernel> -s 2 -c 1 on the
@@ -438,7 +559,7 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS), default="bf16")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + [XL_CONFIG], default="bf16")
     ap.add_argument("--path", choices=["persistent", "kernels"], default="persistent",
                     help="decode step implementation (persistent falls back to kernels where unsupported)")
     ap.add_argument("--quick", action="store_true", help="skip the optional extras (GEMV table, CPU and reference bars)")
@@ -447,6 +568,8 @@ def main():
                          "(the 3rd engine launch); prints no bench line")
     args = ap.parse_args()
     rank, local_rank, world = env_rank()
+    if args.config == XL_CONFIG and args.impl == "ours":
+        return run_xl_tp(args, rank, local_rank, world)
     if args.profile_case:
         return run_profile_case(args)
     if args.impl == "reference":

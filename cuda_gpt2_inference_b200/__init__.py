@@ -101,6 +101,10 @@ _SIGS = {
     "gpt2b_engine_set_position": (_I, [_P, _I, _I]),
     "gpt2b_engine_history": (_I, [_P, _P, _I, _I]),
     "gpt2b_engine_kernels_per_step": (_I, [_P, _P]),
+    "gpt2b_nccl_unique_id": (_I, [_P]),
+    "gpt2b_tp_plan": (_I, [_P, _I, _I, _P]),
+    "gpt2b_tp_shard_image": (_I, [_P, _SZ, _P, _SZ, _I, _I, _I, _P, _P, _P, _P]),
+    "gpt2b_engine_create_tp_from_buffer": (_I, [_P, _SZ, _P, _SZ, _I, _I, _I, _I, _P, _P]),
 }
 
 _lib = None

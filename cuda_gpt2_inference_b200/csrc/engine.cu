@@ -27,6 +27,10 @@
 #include "common.cuh"
 #include "internal.h"
 
+#if GPT2B_HAVE_NCCL
+#include <nccl.h>
+#endif
+
 #include <math.h>
 #include <stdio.h>
 #include <string.h>
@@ -77,6 +81,17 @@ struct gpt2b_engine {
     unsigned char* xchg = nullptr;
     size_t xchg_bytes = 0;
     PersistParams pp;
+    // tensor parallelism (tp_size 1: single GPU): this rank's heads, FC rows and vocab rows
+    int tp_rank = 0, tp_size = 1;
+    int h0 = 0, nh_l = 0, f0 = 0, f_l = 0, v0 = 0, v_rows = 0;
+    float* proj_f32 = nullptr;     // row-parallel partial sums (C floats), all-reduced in place
+    float* fcproj_f32 = nullptr;
+    float* lm_pair = nullptr;      // (best logit, global index) of this rank's vocab rows
+    float* lm_pairs = nullptr;     // every rank's pair
+    float* logits_full = nullptr;  // all-gathered logits (Vp) for host copies and sampling
+#if GPT2B_HAVE_NCCL
+    ncclComm_t comm = nullptr;
+#endif
 };
 
 namespace {
@@ -106,6 +121,110 @@ void param_sizes(const gpt2b_config& c, size_t n[16]) {
 // tensors stored as 8-bit codes in the mixed file (quantize.cu:190-196)
 const int kLinearSlot[16] = {0, -1, -1, -1, 1, -1, 2, -1, -1, -1, 3, -1, 4, -1, -1, -1};
 
+// Tensor-parallel shard of one rank (SURVEY-style Megatron split for decode):
+// QKV and FC column-parallel (heads, FC rows), attention projection and FC
+// projection row-parallel (their K slices), LM head vocab-parallel.  25 heads
+// split unevenly (13/12, 7/6/6/6, 4/3x7); FC rows and vocab rows evenly.
+struct TpPlan {
+    int h0, nh_l, f0, f_l, v0, v_rows;
+};
+bool tp_plan(const gpt2b_config& c, int rank, int size, TpPlan* pl) {
+    const int NH = c.num_heads, F = 4 * c.channels, Vp = c.padded_vocab_size;
+    if (size < 1 || rank < 0 || rank >= size || size > NH) return false;
+    if (size > 1 && (F % (16 * size) != 0 || Vp % size != 0)) return false;
+    const int q = NH / size, r = NH % size;
+    pl->nh_l = q + (rank < r ? 1 : 0);
+    pl->h0 = rank * q + (rank < r ? rank : r);
+    pl->f_l = F / size;
+    pl->f0 = rank * pl->f_l;
+    pl->v_rows = Vp / size;
+    pl->v0 = rank * pl->v_rows;
+    return true;
+}
+
+// Element counts of this rank's 16 parameter tensors and 5 scale arrays.
+void local_sizes(const gpt2b_config& c, const TpPlan& pl, size_t n[16], size_t ns[5]) {
+    const size_t C = c.channels, L = c.num_layers, Vp = c.padded_vocab_size, maxT = c.max_seq_len;
+    const size_t Q = 3 * (size_t)pl.nh_l * 64, A = (size_t)pl.nh_l * 64, F = pl.f_l;
+    const size_t v[16] = {Vp * C, maxT * C, L * C, L * C, L * Q * C, L * Q, L * C * A, L * C,
+                          L * C, L * C, L * F * C, L * F, L * C * F, L * C, C, C};
+    for (int i = 0; i < 16; i++) n[i] = v[i];
+    const size_t w[5] = {Vp, L * Q, L * C, L * F, L * C};
+    for (int g = 0; g < 5; g++) ns[g] = w[g];
+}
+
+// Copies this rank's slices of the full (file-order) tensors into `out`
+// (local tensors in file order, element sizes as stored) and of the scale
+// groups into `out_sc`.  Row-parallel biases are kept by rank 0 only (the
+// other ranks hold zeros) so the all-reduced sum carries them once.
+void tp_shard(const unsigned char* image, const float* scales, const gpt2b_config& c, bool w8, size_t xb,
+              const TpPlan& pl, int rank, std::vector<unsigned char>& out, std::vector<float>& out_sc) {
+    const size_t C = c.channels, L = c.num_layers, NH64 = (size_t)c.num_heads * 64, F4 = 4 * C;
+    size_t nf[16], nl[16], nsl[5];
+    param_sizes(c, nf);
+    local_sizes(c, pl, nl, nsl);
+    size_t total = 0;
+    for (int i = 0; i < 16; i++) total += nl[i] * ((w8 && kLinearSlot[i] >= 0) ? 1 : xb);
+    out.assign(total, 0);
+    const unsigned char* src = image + 1024;
+    unsigned char* dst = out.data();
+    const size_t h0 = (size_t)pl.h0 * 64, hl = (size_t)pl.nh_l * 64, f0 = pl.f0, fl = pl.f_l;
+    for (int i = 0; i < 16; i++) {
+        const size_t eb = (w8 && kLinearSlot[i] >= 0) ? 1 : xb;
+        auto rows = [&](size_t nrow_full, size_t r0, size_t nr, size_t row_elems) {  // [L][nrow_full][row]
+            for (size_t l = 0; l < L; l++) {
+                memcpy(dst, src + (l * nrow_full + r0) * row_elems * eb, nr * row_elems * eb);
+                dst += nr * row_elems * eb;
+            }
+        };
+        auto cols = [&](size_t nrow, size_t ncol_full, size_t k0, size_t nk) {  // [L][nrow][ncol_full]
+            for (size_t l = 0; l < L; l++)
+                for (size_t r = 0; r < nrow; r++) {
+                    memcpy(dst, src + ((l * nrow + r) * ncol_full + k0) * eb, nk * eb);
+                    dst += nk * eb;
+                }
+        };
+        switch (i) {
+            case 4:  // qkvw [L][3C][C]: q, k, v rows of this rank's heads
+            case 5:  // qkvb [L][3C]
+                for (size_t l = 0; l < L; l++)
+                    for (size_t part = 0; part < 3; part++) {
+                        const size_t re = (i == 4) ? C : 1;
+                        memcpy(dst, src + ((l * 3 + part) * NH64 + h0) * re * eb, hl * re * eb);
+                        dst += hl * re * eb;
+                    }
+                break;
+            case 6: cols(C, C, h0, hl); break;               // attprojw [L][C][C]: K slice of the heads
+            case 10: rows(F4, f0, fl, C); break;             // fcw [L][4C][C]: FC rows
+            case 11: rows(F4, f0, fl, 1); break;             // fcb [L][4C]
+            case 12: cols(C, F4, f0, fl); break;             // fcprojw [L][C][4C]: K slice
+            case 7:                                          // attprojb, fcprojb: rank 0 only
+            case 13:
+                if (rank == 0) memcpy(dst, src, nf[i] * eb);
+                dst += nf[i] * eb;
+                break;
+            default: memcpy(dst, src, nf[i] * eb); dst += nf[i] * eb; break;
+        }
+        src += nf[i] * eb;
+    }
+    out_sc.clear();
+    if (!w8) return;
+    size_t nsf[5] = {(size_t)c.padded_vocab_size, L * 3 * C, L * C, L * F4, L * C};
+    const float* s = scales;
+    for (int g = 0; g < 5; g++) {
+        if (g == 1) {
+            for (size_t l = 0; l < L; l++)
+                for (size_t part = 0; part < 3; part++)
+                    out_sc.insert(out_sc.end(), s + (l * 3 + part) * NH64 + h0, s + (l * 3 + part) * NH64 + h0 + hl);
+        } else if (g == 3) {
+            for (size_t l = 0; l < L; l++) out_sc.insert(out_sc.end(), s + l * F4 + f0, s + l * F4 + f0 + fl);
+        } else {
+            out_sc.insert(out_sc.end(), s, s + nsf[g]);
+        }
+        s += nsf[g];
+    }
+}
+
 int check_header(const int* hdr, int wmode, gpt2b_config* cfg) {
     if (hdr[0] != 20251103) return GPT2B_ERR_FORMAT;
     const int want = (wmode == GPT2B_W_F32) ? 3 : 5;
@@ -125,8 +244,11 @@ int check_header(const int* hdr, int wmode, gpt2b_config* cfg) {
 void free_engine(gpt2b_engine* e) {
     if (!e) return;
     DeviceGuard g(e->device);
-    if (e->graph_multi) cudaGraphExecDestroy(e->graph_multi);
+    if (e->graph_multi) cudaGraphExecDestroy(e->graph_multi);  // graphs holding collectives go first
     if (e->graph_one) cudaGraphExecDestroy(e->graph_one);
+#if GPT2B_HAVE_NCCL
+    if (e->comm) ncclCommDestroy(e->comm);
+#endif
     if (e->params) cudaFree(e->params);
     if (e->acts) cudaFree(e->acts);
     if (e->kv) cudaFree(e->kv);
@@ -135,27 +257,75 @@ void free_engine(gpt2b_engine* e) {
     delete e;
 }
 
-// Launches one decode step (5L + 1 kernels) on e->stream.
+// Picks the next token from every tensor-parallel rank's (best logit, global
+// index) pair -- first maximum, lowest index on ties, the order the
+// single-GPU LM head uses -- and advances token, position and history.
+__global__ void tp_pick_kernel(const float* pairs, int n, const int* prompt, int n_prompt, int* token, int* pos,
+                               int* history) {
+    float bv = pairs[0];
+    int bi = __float_as_int(pairs[1]);
+    for (int r = 1; r < n; r++) {
+        const float v = pairs[2 * r];
+        const int i = __float_as_int(pairs[2 * r + 1]);
+        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+    }
+    const int p = *pos;
+    const int next = (p + 1 < n_prompt) ? prompt[p + 1] : bi;
+    history[p + 1] = next;
+    *token = next;
+    *pos = p + 1;
+}
+
+// Sum of this rank's FP32 partials over the tensor-parallel group, in place.
+cudaError_t tp_allreduce(gpt2b_engine* e, float* buf, size_t n) {
+#if GPT2B_HAVE_NCCL
+    return ncclAllReduce(buf, buf, n, ncclFloat, ncclSum, e->comm, e->stream) == ncclSuccess ? cudaSuccess
+                                                                                           : cudaErrorUnknown;
+#else
+    (void)e; (void)buf; (void)n;
+    return cudaErrorNotSupported;
+#endif
+}
+cudaError_t tp_allgather(gpt2b_engine* e, const float* send, float* recv, size_t n) {
+#if GPT2B_HAVE_NCCL
+    return ncclAllGather(send, recv, n, ncclFloat, e->comm, e->stream) == ncclSuccess ? cudaSuccess
+                                                                                    : cudaErrorUnknown;
+#else
+    (void)e; (void)send; (void)recv; (void)n;
+    return cudaErrorNotSupported;
+#endif
+}
+
+// Launches one decode step (5L + 1 kernels; with tensor parallelism also 2L
+// all-reduces, the pair all-gather and the pick) on e->stream.
 cudaError_t launch_step(gpt2b_engine* e) {
-    const int L = e->cfg.num_layers;
+    const int L = e->cfg.num_layers, C = e->cfg.channels;
+    const bool tp = e->tp_size > 1;
     const bool pdl = e->use_pdl;
     cudaError_t err;
     for (int l = 0; l < L; l++) {
-        err = launch_gemv(e->qkv_p[l], e->wk, false, l == 0 ? PRO_EMB_LN : PRO_RES_LN, EPI_STORE, e->stream, pdl);
+        err = launch_gemv(e->qkv_p[l], e->wk, false, l == 0 ? PRO_EMB_LN : PRO_RES_LN, EPI_STORE, e->stream,
+                          pdl && !(tp && l > 0));
         if (err != cudaSuccess) return err;
         unsigned char* kv_l = e->kv_cache + (size_t)l * e->kv_layer_elems * (e->kvk >= KV_I8 ? 1 : e->xbytes);
         float* ks_l = e->kv_scale ? e->kv_scale + (size_t)l * e->kv_layer_scales : nullptr;
-        err = launch_attention_engine(e->kvk, e->qkv, kv_l, ks_l, e->d_pos, e->cfg.num_heads, e->cfg.max_seq_len,
+        err = launch_attention_engine(e->kvk, e->qkv, kv_l, ks_l, e->d_pos, e->nh_l, e->cfg.max_seq_len,
                                       e->splits, e->part_out, e->part_max, e->part_lse, e->stream, pdl);
         if (err != cudaSuccess) return err;
-        err = launch_gemv(e->proj_p[l], e->wk, false, PRO_ATTN_MERGE, EPI_STORE, e->stream, pdl);
+        err = launch_gemv(e->proj_p[l], e->wk, tp, PRO_ATTN_MERGE, EPI_STORE, e->stream, pdl);
         if (err != cudaSuccess) return err;
-        err = launch_gemv(e->fc_p[l], e->wk, false, PRO_RES_LN, EPI_STORE, e->stream, pdl);
+        if (tp && (err = tp_allreduce(e, e->proj_f32, C)) != cudaSuccess) return err;
+        err = launch_gemv(e->fc_p[l], e->wk, false, PRO_RES_LN, EPI_STORE, e->stream, pdl && !tp);
         if (err != cudaSuccess) return err;
-        err = launch_gemv(e->fcproj_p[l], e->wk, false, PRO_PLAIN, EPI_STORE, e->stream, pdl);
+        err = launch_gemv(e->fcproj_p[l], e->wk, tp, PRO_PLAIN, EPI_STORE, e->stream, pdl);
         if (err != cudaSuccess) return err;
+        if (tp && (err = tp_allreduce(e, e->fcproj_f32, C)) != cudaSuccess) return err;
     }
-    return launch_gemv(e->lm_p, e->wk, true, PRO_RES_LN, EPI_LMHEAD, e->stream, pdl);
+    err = launch_gemv(e->lm_p, e->wk, true, PRO_RES_LN, EPI_LMHEAD, e->stream, pdl && !tp);
+    if (err != cudaSuccess || !tp) return err;
+    if ((err = tp_allgather(e, e->lm_pair, e->lm_pairs, 2)) != cudaSuccess) return err;
+    return launch_k(tp_pick_kernel, dim3(1), dim3(1), 0, e->stream, false, (const float*)e->lm_pairs, e->tp_size,
+                    (const int*)e->d_prompt, e->lm_p.n_prompt, e->d_token, e->d_pos, e->d_history);
 }
 
 cudaError_t capture(gpt2b_engine* e, int steps, cudaGraphExec_t* out) {
@@ -224,6 +394,7 @@ __global__ void set_history_kernel(int* history, const int* d_token, const int* 
 // arena: tagged words per layer and phase, per-(layer, head) KV flags, the
 // epoch counter and the abort flag.
 cudaError_t setup_persistent(gpt2b_engine* e, int nsm) {
+    if (e->tp_size > 1) return cudaSuccess;  // tensor parallel: per-kernel path with collectives
     const gpt2b_config& c = e->cfg;
     const int C = c.channels, NH = c.num_heads, L = c.num_layers, maxT = c.max_seq_len;
     int coop = 0;
@@ -279,7 +450,7 @@ cudaError_t setup_persistent(gpt2b_engine* e, int nsm) {
 }
 
 int build_engine(const unsigned char* image, size_t nbytes, const float* scales, size_t nscales, int wmode,
-                 int kvmode, gpt2b_engine** out) {
+                 int kvmode, int tp_rank, int tp_size, const void* nccl_id, gpt2b_engine** out) {
     if (!out) return GPT2B_ERR_INVALID_ARG;
     *out = nullptr;
     if (wmode < GPT2B_W_F32 || wmode > GPT2B_W_FP8 || (kvmode != GPT2B_KV_FLOATX && kvmode != GPT2B_KV_8BIT))
@@ -304,6 +475,25 @@ int build_engine(const unsigned char* image, size_t nbytes, const float* scales,
     if (nbytes != file_bytes) return GPT2B_ERR_FORMAT;
     const size_t n_scales = (size_t)Vp + (size_t)L * 3 * C + (size_t)L * C + (size_t)L * 4 * C + (size_t)L * C;
     if (w8 && (!scales || nscales != n_scales)) return GPT2B_ERR_FORMAT;
+    TpPlan pl;
+    if (!tp_plan(cfg, tp_rank, tp_size, &pl)) return GPT2B_ERR_UNSUPPORTED;
+#if !GPT2B_HAVE_NCCL
+    if (tp_size > 1) return GPT2B_ERR_UNSUPPORTED;
+#endif
+    if (tp_size > 1 && !nccl_id) return GPT2B_ERR_INVALID_ARG;
+    size_t nl[16], nsl[5];
+    local_sizes(cfg, pl, nl, nsl);
+    // this rank's tensors (the image itself on a single GPU)
+    std::vector<unsigned char> shard;
+    std::vector<float> shard_sc;
+    const unsigned char* src_params = image + 1024;
+    const float* src_scales = scales;
+    if (tp_size > 1) {
+        tp_shard(image, scales, cfg, w8, xb, pl, tp_rank, shard, shard_sc);
+        src_params = shard.data();
+        src_scales = shard_sc.data();
+    }
+    const int NHl = pl.nh_l, Fl = pl.f_l;
 
     gpt2b_engine* e = new gpt2b_engine();
     cudaGetDevice(&e->device);
@@ -313,6 +503,9 @@ int build_engine(const unsigned char* image, size_t nbytes, const float* scales,
     e->w8 = w8;
     e->xbytes = xb;
     e->wk = (wmode == GPT2B_W_F32) ? WK_F32 : (wmode == GPT2B_W_BF16 ? WK_BF16 : (wmode == GPT2B_W_INT8 ? WK_I8 : WK_FP8));
+    e->tp_rank = tp_rank;
+    e->tp_size = tp_size;
+    e->h0 = pl.h0; e->nh_l = pl.nh_l; e->f0 = pl.f0; e->f_l = pl.f_l; e->v0 = pl.v0; e->v_rows = pl.v_rows;
     if (kvmode == GPT2B_KV_8BIT) e->kvk = (wmode == GPT2B_W_FP8) ? KV_FP8 : KV_I8;
     else e->kvk = (wmode == GPT2B_W_F32) ? KV_F32 : KV_BF16;
 
@@ -320,38 +513,49 @@ int build_engine(const unsigned char* image, size_t nbytes, const float* scales,
     auto fail = [&](cudaError_t x) { free_engine(e); return status_from(x); };
     if (err != cudaSuccess) return fail(err);
 
-    // ---- parameter arena ----
+#if GPT2B_HAVE_NCCL
+    if (tp_size > 1) {  // collective: every rank of the group calls this together
+        ncclUniqueId id;
+        memcpy(&id, nccl_id, sizeof(id));
+        if (ncclCommInitRank(&e->comm, tp_size, id, tp_rank) != ncclSuccess) {
+            e->comm = nullptr;
+            free_engine(e);
+            return GPT2B_ERR_NCCL;
+        }
+    }
+#endif
+
+    // ---- parameter arena (this rank's shard) ----
     size_t off[16], total = 0;
     for (int i = 0; i < 16; i++) {
         off[i] = total;
-        total = align256(total + n[i] * ((w8 && kLinearSlot[i] >= 0) ? 1 : xb));
+        total = align256(total + nl[i] * ((w8 && kLinearSlot[i] >= 0) ? 1 : xb));
     }
     size_t sc_off[5];
-    const size_t sc_n[5] = {(size_t)Vp, (size_t)L * 3 * C, (size_t)L * C, (size_t)L * 4 * C, (size_t)L * C};
     if (w8)
-        for (int g = 0; g < 5; g++) { sc_off[g] = total; total = align256(total + sc_n[g] * 4); }
+        for (int g = 0; g < 5; g++) { sc_off[g] = total; total = align256(total + nsl[g] * 4); }
     e->params_bytes = total;
     if ((err = cudaMalloc(&e->params, total)) != cudaSuccess) return fail(err);
-    const unsigned char* src = image + 1024;
+    const unsigned char* src = src_params;
     for (int i = 0; i < 16; i++) {
-        const size_t b = n[i] * ((w8 && kLinearSlot[i] >= 0) ? 1 : xb);
+        const size_t b = nl[i] * ((w8 && kLinearSlot[i] >= 0) ? 1 : xb);
         e->p[i] = e->params + off[i];
         if ((err = cudaMemcpy(e->p[i], src, b, cudaMemcpyHostToDevice)) != cudaSuccess) return fail(err);
         src += b;
     }
     if (w8) {
-        const float* s = scales;
+        const float* s = src_scales;
         for (int g = 0; g < 5; g++) {
             e->sc[g] = reinterpret_cast<float*>(e->params + sc_off[g]);
-            if ((err = cudaMemcpy(e->sc[g], s, sc_n[g] * 4, cudaMemcpyHostToDevice)) != cudaSuccess) return fail(err);
-            s += sc_n[g];
+            if ((err = cudaMemcpy(e->sc[g], s, nsl[g] * 4, cudaMemcpyHostToDevice)) != cudaSuccess) return fail(err);
+            s += nsl[g];
         }
     }
 
     // ---- activation arena ----
     const int nsm = sm_count();
     const int max_chunk = attn_engine_max_chunk(e->kvk);
-    int splits = std::max((maxT + max_chunk - 1) / max_chunk, nsm / NH);
+    int splits = std::max((maxT + max_chunk - 1) / max_chunk, nsm / NHl);
     if (splits < 1) splits = 1;
     // engine chunks are multiples of 16 positions and at most max_chunk
     while (splits > 1 && ((((maxT + splits - 1) / splits) + 15) & ~15) > max_chunk) splits++;
@@ -359,16 +563,20 @@ int build_engine(const unsigned char* image, size_t nbytes, const float* scales,
     const int lm_grid_max = 2 * nsm;
     struct Slot { unsigned char** ptr; size_t bytes; };
     unsigned char *logits_b, *po_b, *pm_b, *pl_b, *lmv_b, *lmi_b, *lmc_b, *tok_b, *pos_b, *hist_b, *pr_b, *np_b;
+    unsigned char *pf_b, *fpf_b, *pair_b, *pairs_b, *lfull_b;
+    const bool tp = tp_size > 1;
     std::vector<Slot> slots = {
-        {&e->encoded, C * xb},        {&e->ln1, (size_t)L * C * xb},   {&e->qkv, 3 * (size_t)C * xb},
-        {&e->atty, (size_t)L * C * xb}, {&e->res2, (size_t)L * C * xb}, {&e->ln2, (size_t)L * C * xb},
-        {&e->fch, (size_t)L * 4 * C * xb}, {&e->fch_gelu, 4 * (size_t)C * xb}, {&e->res3, (size_t)L * C * xb},
+        {&e->encoded, C * xb},        {&e->ln1, (size_t)L * C * xb},   {&e->qkv, 3 * (size_t)NHl * hs * xb},
+        {&e->atty, (size_t)L * NHl * hs * xb}, {&e->res2, (size_t)L * C * xb}, {&e->ln2, (size_t)L * C * xb},
+        {&e->fch, (size_t)L * Fl * xb}, {&e->fch_gelu, (size_t)Fl * xb}, {&e->res3, (size_t)L * C * xb},
         {&e->lnf, C * xb},            {&e->proj_out, C * xb},          {&e->fcproj_out, C * xb},
-        {&logits_b, (size_t)Vp * 4},  {&po_b, (size_t)NH * splits * hs * 4}, {&pm_b, (size_t)NH * splits * 4},
-        {&pl_b, (size_t)NH * splits * 4}, {&lmv_b, (size_t)lm_grid_max * 4},
+        {&logits_b, (size_t)pl.v_rows * 4},  {&po_b, (size_t)NHl * splits * hs * 4}, {&pm_b, (size_t)NHl * splits * 4},
+        {&pl_b, (size_t)NHl * splits * 4}, {&lmv_b, (size_t)lm_grid_max * 4},
         {&lmi_b, (size_t)lm_grid_max * 4}, {&lmc_b, 16},               {&tok_b, 16},
         {&pos_b, 16},                 {&hist_b, (size_t)(maxT + 1) * 4}, {&pr_b, (size_t)maxT * 4},
-        {&np_b, 16}};
+        {&np_b, 16},
+        {&pf_b, tp ? (size_t)C * 4 : 16}, {&fpf_b, tp ? (size_t)C * 4 : 16}, {&pair_b, 16},
+        {&pairs_b, (size_t)tp_size * 8}, {&lfull_b, tp ? (size_t)Vp * 4 : 16}};
     size_t at = 0;
     for (auto& s : slots) at = align256(at + s.bytes);
     e->acts_bytes = at;
@@ -388,10 +596,17 @@ int build_engine(const unsigned char* image, size_t nbytes, const float* scales,
     e->d_history = reinterpret_cast<int*>(hist_b);
     e->d_prompt = reinterpret_cast<int*>(pr_b);
     e->d_nprompt = reinterpret_cast<int*>(np_b);
+    if (tp) {
+        e->proj_f32 = reinterpret_cast<float*>(pf_b);
+        e->fcproj_f32 = reinterpret_cast<float*>(fpf_b);
+        e->lm_pair = reinterpret_cast<float*>(pair_b);
+        e->lm_pairs = reinterpret_cast<float*>(pairs_b);
+        e->logits_full = reinterpret_cast<float*>(lfull_b);
+    }
 
     // ---- KV arena ----
-    e->kv_layer_elems = 2 * (size_t)NH * maxT * hs;
-    e->kv_layer_scales = (e->kvk >= KV_I8) ? 2 * (size_t)NH * maxT : 0;
+    e->kv_layer_elems = 2 * (size_t)NHl * maxT * hs;
+    e->kv_layer_scales = (e->kvk >= KV_I8) ? 2 * (size_t)NHl * maxT : 0;
     const size_t kv_elem_b = (e->kvk >= KV_I8) ? 1 : xb;
     size_t kvb = align256((size_t)L * e->kv_layer_elems * kv_elem_b);
     const size_t sc_at = kvb;
@@ -409,13 +624,14 @@ int build_engine(const unsigned char* image, size_t nbytes, const float* scales,
     e->proj_p.resize(L);
     e->fc_p.resize(L);
     e->fcproj_p.resize(L);
+    const size_t Q = 3 * (size_t)NHl * hs, A = (size_t)NHl * hs;  // local QKV rows, projection K
     for (int l = 0; l < L; l++) {
         GemvParams q;
-        q.W = e->p[4] + (size_t)l * 3 * C * C * wb;
-        q.scale = w8 ? e->sc[1] + (size_t)l * 3 * C : nullptr;
-        q.bias = e->p[5] + (size_t)l * 3 * C * xb;
+        q.W = e->p[4] + (size_t)l * Q * C * wb;
+        q.scale = w8 ? e->sc[1] + (size_t)l * Q : nullptr;
+        q.bias = e->p[5] + (size_t)l * Q * xb;
         q.out = e->qkv;
-        q.M = 3 * C; q.K = C;
+        q.M = (int)Q; q.K = C;
         q.ln_w = e->p[2] + (size_t)l * C * xb;
         q.ln_b = e->p[3] + (size_t)l * C * xb;
         q.ln_out = e->ln1 + (size_t)l * C * xb;
@@ -429,39 +645,41 @@ int build_engine(const unsigned char* image, size_t nbytes, const float* scales,
             q.res_out = e->encoded;
         } else {
             q.res_in = e->res2 + (size_t)(l - 1) * C * xb;
-            q.delta = e->fcproj_out;
+            q.delta = tp ? (const void*)e->fcproj_f32 : (const void*)e->fcproj_out;
+            q.delta_f32 = tp ? 1 : 0;
             q.res_out = e->res3 + (size_t)(l - 1) * C * xb;
         }
         plan_gemv(q, wk, nsm, true);
         e->qkv_p[l] = q;
 
         GemvParams pr;
-        pr.W = e->p[6] + (size_t)l * C * C * wb;
+        pr.W = e->p[6] + (size_t)l * C * A * wb;
         pr.scale = w8 ? e->sc[2] + (size_t)l * C : nullptr;
         pr.bias = e->p[7] + (size_t)l * C * xb;
         pr.part_out = e->part_out;  // x = merge of the attention partials (PRO_ATTN_MERGE)
         pr.part_max = e->part_max;
         pr.part_lse = e->part_lse;
-        pr.attn_heads = NH;
+        pr.attn_heads = NHl;
         pr.attn_splits = splits;
         pr.d_pos = e->d_pos;
-        pr.atty_out = e->atty + (size_t)l * C * xb;
-        pr.aux_bytes = NH * splits * 64 * 4 + 2 * (((NH * splits * 4) + 15) & ~15);
-        pr.out = e->proj_out;
-        pr.M = C; pr.K = C;
+        pr.atty_out = e->atty + (size_t)l * A * xb;
+        pr.aux_bytes = NHl * splits * 64 * 4 + 2 * (((NHl * splits * 4) + 15) & ~15);
+        pr.out = tp ? (void*)e->proj_f32 : (void*)e->proj_out;  // row-parallel: FP32 partial sums
+        pr.M = C; pr.K = (int)A;
         plan_gemv(pr, wk, nsm, true);
         e->proj_p[l] = pr;
 
         GemvParams f;
-        f.W = e->p[10] + (size_t)l * 4 * C * C * wb;
-        f.scale = w8 ? e->sc[3] + (size_t)l * 4 * C : nullptr;
-        f.bias = e->p[11] + (size_t)l * 4 * C * xb;
+        f.W = e->p[10] + (size_t)l * Fl * C * wb;
+        f.scale = w8 ? e->sc[3] + (size_t)l * Fl : nullptr;
+        f.bias = e->p[11] + (size_t)l * Fl * xb;
         f.out = e->fch_gelu;
-        f.pre_gelu = e->fch + (size_t)l * 4 * C * xb;
+        f.pre_gelu = e->fch + (size_t)l * Fl * xb;
         f.do_gelu = 1;
-        f.M = 4 * C; f.K = C;
+        f.M = Fl; f.K = C;
         f.res_in = (l == 0) ? e->encoded : e->res3 + (size_t)(l - 1) * C * xb;
-        f.delta = e->proj_out;
+        f.delta = tp ? (const void*)e->proj_f32 : (const void*)e->proj_out;
+        f.delta_f32 = tp ? 1 : 0;
         f.res_out = e->res2 + (size_t)l * C * xb;
         f.ln_out = e->ln2 + (size_t)l * C * xb;
         f.ln_w = e->p[8] + (size_t)l * C * xb;
@@ -470,28 +688,30 @@ int build_engine(const unsigned char* image, size_t nbytes, const float* scales,
         e->fc_p[l] = f;
 
         GemvParams fp;
-        fp.W = e->p[12] + (size_t)l * C * 4 * C * wb;
+        fp.W = e->p[12] + (size_t)l * C * Fl * wb;
         fp.scale = w8 ? e->sc[4] + (size_t)l * C : nullptr;
         fp.bias = e->p[13] + (size_t)l * C * xb;
         fp.x = e->fch_gelu;
-        fp.out = e->fcproj_out;
-        fp.M = C; fp.K = 4 * C;
+        fp.out = tp ? (void*)e->fcproj_f32 : (void*)e->fcproj_out;
+        fp.M = C; fp.K = Fl;
         plan_gemv(fp, wk, nsm, true);
         e->fcproj_p[l] = fp;
     }
-    GemvParams lm;
-    lm.W = e->p[0];
-    lm.scale = w8 ? e->sc[0] : nullptr;
+    GemvParams lm;  // this rank's vocab rows [v0, v0 + v_rows) of the tied wte
+    lm.W = e->p[0] + (size_t)pl.v0 * C * wb;
+    lm.scale = w8 ? e->sc[0] + pl.v0 : nullptr;
     lm.out = e->logits;
-    lm.M = Vp; lm.K = C;
+    lm.M = pl.v_rows; lm.K = C;
     lm.res_in = e->res2 + (size_t)(L - 1) * C * xb;
-    lm.delta = e->fcproj_out;
+    lm.delta = tp ? (const void*)e->fcproj_f32 : (const void*)e->fcproj_out;
+    lm.delta_f32 = tp ? 1 : 0;
     lm.res_out = e->res3 + (size_t)(L - 1) * C * xb;
     lm.ln_out = e->lnf;
     lm.ln_w = e->p[14];
     lm.ln_b = e->p[15];
-    lm.vocab = cfg.vocab_size;
+    lm.vocab = std::max(0, std::min(cfg.vocab_size - pl.v0, pl.v_rows));  // valid rows of the shard
     lm.part_val = e->lm_val; lm.part_idx = e->lm_idx; lm.counter = e->lm_counter;
+    if (tp) { lm.pair_out = e->lm_pair; lm.row_offset = pl.v0; }
     lm.token_io = e->d_token; lm.pos_io = e->d_pos; lm.history = e->d_history;
     lm.prompt = e->d_prompt;
     lm.n_prompt = 0;
@@ -544,7 +764,79 @@ int gpt2b_read_header(const char* path, int* version, gpt2b_config* cfg) {
 
 int gpt2b_engine_create_from_buffer(const void* image, size_t nbytes, const float* scales, size_t nscales, int wmode,
                                     int kvmode, gpt2b_engine** out) {
-    return build_engine(static_cast<const unsigned char*>(image), nbytes, scales, nscales, wmode, kvmode, out);
+    return build_engine(static_cast<const unsigned char*>(image), nbytes, scales, nscales, wmode, kvmode, 0, 1, nullptr,
+                        out);
+}
+
+int gpt2b_engine_create_tp_from_buffer(const void* image, size_t nbytes, const float* scales, size_t nscales,
+                                       int wmode, int kvmode, int tp_rank, int tp_size, const void* nccl_id,
+                                       gpt2b_engine** out) {
+    return build_engine(static_cast<const unsigned char*>(image), nbytes, scales, nscales, wmode, kvmode, tp_rank,
+                        tp_size, nccl_id, out);
+}
+
+int gpt2b_nccl_unique_id(void* id_out) {
+    if (!id_out) return GPT2B_ERR_INVALID_ARG;
+#if GPT2B_HAVE_NCCL
+    ncclUniqueId id;
+    if (ncclGetUniqueId(&id) != ncclSuccess) return GPT2B_ERR_NCCL;
+    memcpy(id_out, &id, sizeof(id));
+    return GPT2B_OK;
+#else
+    return GPT2B_ERR_UNSUPPORTED;
+#endif
+}
+
+int gpt2b_tp_plan(const gpt2b_config* cfg, int tp_rank, int tp_size, int* out6) {
+    if (!cfg || !out6) return GPT2B_ERR_INVALID_ARG;
+    TpPlan pl;
+    if (!tp_plan(*cfg, tp_rank, tp_size, &pl)) return GPT2B_ERR_UNSUPPORTED;
+    const int v[6] = {pl.h0, pl.nh_l, pl.f0, pl.f_l, pl.v0, pl.v_rows};
+    memcpy(out6, v, sizeof(v));
+    return GPT2B_OK;
+}
+
+int gpt2b_tp_shard_image(const void* image, size_t nbytes, const float* scales, size_t nscales, int wmode,
+                         int tp_rank, int tp_size, void* out_params, size_t* out_bytes, float* out_scales,
+                         size_t* out_nscales) {
+    if (!image || !out_bytes || !out_nscales || nbytes < 1024) return GPT2B_ERR_INVALID_ARG;
+    if (wmode < GPT2B_W_F32 || wmode > GPT2B_W_FP8) return GPT2B_ERR_INVALID_ARG;
+    const bool w8 = (wmode == GPT2B_W_INT8 || wmode == GPT2B_W_FP8);
+    int hdr[256];
+    memcpy(hdr, image, sizeof(hdr));
+    gpt2b_config cfg;
+    int rc = check_header(hdr, wmode, &cfg);
+    if (rc) return rc;
+    size_t n[16];
+    param_sizes(cfg, n);
+    const size_t xb = (wmode == GPT2B_W_F32) ? 4 : 2;
+    size_t file_bytes = 1024;
+    for (int i = 0; i < 16; i++) file_bytes += n[i] * ((w8 && kLinearSlot[i] >= 0) ? 1 : xb);
+    if (nbytes != file_bytes) return GPT2B_ERR_FORMAT;
+    const size_t C = cfg.channels, L = cfg.num_layers;
+    const size_t n_scales = (size_t)cfg.padded_vocab_size + L * 3 * C + L * C + L * 4 * C + L * C;
+    if (w8 && (!scales || nscales != n_scales)) return GPT2B_ERR_FORMAT;
+    TpPlan pl;
+    if (!tp_plan(cfg, tp_rank, tp_size, &pl)) return GPT2B_ERR_UNSUPPORTED;
+    size_t nl[16], nsl[5], total = 0, total_sc = 0;
+    local_sizes(cfg, pl, nl, nsl);
+    for (int i = 0; i < 16; i++) total += nl[i] * ((w8 && kLinearSlot[i] >= 0) ? 1 : xb);
+    if (w8)
+        for (int g = 0; g < 5; g++) total_sc += nsl[g];
+    if (!out_params) {  // size query
+        *out_bytes = total;
+        *out_nscales = total_sc;
+        return GPT2B_OK;
+    }
+    if (*out_bytes < total || (w8 && (!out_scales || *out_nscales < total_sc))) return GPT2B_ERR_INVALID_ARG;
+    std::vector<unsigned char> sh;
+    std::vector<float> ssc;
+    tp_shard(static_cast<const unsigned char*>(image), scales, cfg, w8, xb, pl, tp_rank, sh, ssc);
+    memcpy(out_params, sh.data(), sh.size());
+    if (w8) memcpy(out_scales, ssc.data(), ssc.size() * sizeof(float));
+    *out_bytes = total;
+    *out_nscales = total_sc;
+    return GPT2B_OK;
 }
 
 int gpt2b_engine_create_from_file(const char* model_path, const char* scale_path, int wmode, int kvmode,
@@ -566,7 +858,7 @@ int gpt2b_engine_create_from_file(const char* model_path, const char* scale_path
         if (sc.size() % 4) return GPT2B_ERR_FORMAT;
     }
     return build_engine(img.data(), img.size(), w8 ? reinterpret_cast<const float*>(sc.data()) : nullptr,
-                        sc.size() / 4, wmode, kvmode, out);
+                        sc.size() / 4, wmode, kvmode, 0, 1, nullptr, out);
 }
 
 int gpt2b_engine_destroy(gpt2b_engine* e) {
@@ -620,7 +912,7 @@ int gpt2b_engine_stream(const gpt2b_engine* e, gpt2b_stream_t* stream) {
 
 int gpt2b_engine_device_buffers(const gpt2b_engine* e, float** logits, int** token, int** pos, int** history) {
     if (!e) return GPT2B_ERR_INVALID_ARG;
-    if (logits) *logits = e->logits;
+    if (logits) *logits = e->tp_size > 1 ? e->logits_full : e->logits;
     if (token) *token = e->d_token;
     if (pos) *pos = e->d_pos;
     if (history) *history = e->d_history;
@@ -629,7 +921,7 @@ int gpt2b_engine_device_buffers(const gpt2b_engine* e, float** logits, int** tok
 
 int gpt2b_engine_kernels_per_step(const gpt2b_engine* e, int* n) {
     if (!e || !n) return GPT2B_ERR_INVALID_ARG;
-    *n = e->use_persistent ? 0 : 5 * e->cfg.num_layers + 1;
+    *n = e->use_persistent ? 0 : 5 * e->cfg.num_layers + 1 + (e->tp_size > 1 ? 1 : 0);
     return GPT2B_OK;
 }
 
@@ -642,6 +934,7 @@ int gpt2b_engine_forward(gpt2b_engine* e, int token, int pos) {
     cudaError_t err = cudaMemcpyAsync(e->d_token, &tp[0], sizeof(int), cudaMemcpyHostToDevice, e->stream);
     if (err == cudaSuccess) err = cudaMemcpyAsync(e->d_pos, &tp[1], sizeof(int), cudaMemcpyHostToDevice, e->stream);
     if (err == cudaSuccess) err = run_steps(e, 1);
+    if (err == cudaSuccess && e->tp_size > 1) err = tp_allgather(e, e->logits, e->logits_full, (size_t)e->v_rows);
     if (err == cudaSuccess) err = cudaStreamSynchronize(e->stream);
     return status_from(err);
 }
@@ -695,15 +988,20 @@ int gpt2b_engine_generate(gpt2b_engine* e, const int* prompt, int n_prompt, int 
         } else {
             for (int s = 0; s < total && err == cudaSuccess; s++) {
                 err = run_steps(e, 1);
+                float* lg = e->logits;  // all Vp logits (tensor parallel: gathered from the vocab shards)
+                if (err == cudaSuccess && e->tp_size > 1) {
+                    err = tp_allgather(e, e->logits, e->logits_full, (size_t)e->v_rows);
+                    lg = e->logits_full;
+                }
                 if (err == cudaSuccess && sample && s + 1 >= n_prompt) {
-                    // replace the greedy pick by a softmax sample (step = position of the new token)
-                    int rc = gpt2b_gpu_sample_softmax(e->d_token, e->logits, 1, V, seed, s + 1, (gpt2b_stream_t)st);
+                    // replace the greedy pick by a softmax sample (step = position of the new token);
+                    // every rank draws the same (seed, step) sample from the same logits
+                    int rc = gpt2b_gpu_sample_softmax(e->d_token, lg, 1, V, seed, s + 1, (gpt2b_stream_t)st);
                     if (rc) return rc;
                     err = launch_k(set_history_kernel, dim3(1), dim3(1), 0, st, false, e->d_history, e->d_token, e->d_pos);
                 }
                 if (err == cudaSuccess && logits_host)
-                    err = cudaMemcpyAsync(logits_host + (size_t)s * Vp, e->logits, (size_t)Vp * 4,
-                                          cudaMemcpyDeviceToHost, st);
+                    err = cudaMemcpyAsync(logits_host + (size_t)s * Vp, lg, (size_t)Vp * 4, cudaMemcpyDeviceToHost, st);
             }
         }
     }

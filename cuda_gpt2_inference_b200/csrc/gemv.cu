@@ -266,7 +266,8 @@ __device__ bool build_x(const GemvParams& p, unsigned char* xs, unsigned char* a
             if (tok < 0 || tok >= p.vocab) { if (tid == 0) report_device_error(GPT2B_DEVERR_BAD_TOKEN); tok = 0; }
             if (pos < 0 || pos >= p.maxT) { if (tid == 0) report_device_error(GPT2B_DEVERR_BAD_POS); pos = 0; }
         }
-        uint4 ra[kLnChunks], rb[kLnChunks];
+        uint4 ra[kLnChunks], rb[kLnChunks], rb2[kLnChunks];
+        const bool df32 = (PRO == PRO_RES_LN) && p.delta_f32 && E == 8;  // FP32 delta under BF16 activations
 #pragma unroll
         for (int j = 0; j < kLnChunks; j++) {  // issue every load before using any
             const int c = tid + j * kConsumers;
@@ -275,7 +276,12 @@ __device__ bool build_x(const GemvParams& p, unsigned char* xs, unsigned char* a
                     rb[j] = reinterpret_cast<const uint4*>(reinterpret_cast<const XT*>(p.wpe) + (size_t)pos * C)[c];
                 } else {
                     ra[j] = reinterpret_cast<const uint4*>(p.res_in)[c];
-                    rb[j] = reinterpret_cast<const uint4*>(p.delta)[c];
+                    if (df32) {
+                        rb[j] = reinterpret_cast<const uint4*>(p.delta)[2 * c];
+                        rb2[j] = reinterpret_cast<const uint4*>(p.delta)[2 * c + 1];
+                    } else {
+                        rb[j] = reinterpret_cast<const uint4*>(p.delta)[c];
+                    }
                 }
             }
         }
@@ -288,7 +294,14 @@ __device__ bool build_x(const GemvParams& p, unsigned char* xs, unsigned char* a
                 float a[E], b[E];
                 if constexpr (PRO == PRO_EMB_LN) emb_chunk<WK, XT>(p, tok, c, a);
                 else Vec<XT>::unpack(ra[j], a);
-                Vec<XT>::unpack(rb[j], b);
+                if (df32) {  // the all-reduced FP32 sum, rounded as the single-GPU GEMV stores it
+                    Vec<float>::unpack(rb[j], b);
+                    Vec<float>::unpack(rb2[j], b + 4);
+#pragma unroll
+                    for (int e = 0; e < E; e++) b[e] = round_to<XT>(b[e]);
+                } else {
+                    Vec<XT>::unpack(rb[j], b);
+                }
 #pragma unroll
                 for (int e = 0; e < E; e++) {
                     v[j][e] = round_to<XT>(a[e] + b[e]);
@@ -375,7 +388,10 @@ __device__ void lmhead_finish(const GemvParams& p, float best_v, int best_i, flo
         for (int w = 1; w < kConsumerWarps; w++)
             if (sv[w] > sv[0] || (sv[w] == sv[0] && si[w] < si[0])) { sv[0] = sv[w]; si[0] = si[w]; }
         *p.counter = 0u;
-        if (p.advance) {
+        if (p.pair_out) {  // vocab shard of a tensor-parallel rank: (best, global index) for the all-gather
+            p.pair_out[0] = sv[0];
+            p.pair_out[1] = __int_as_float(si[0] == 0x7fffffff ? si[0] : si[0] + p.row_offset);
+        } else if (p.advance) {
             const int pos = *p.pos_io;
             const int next = (pos + 1 < p.n_prompt) ? p.prompt[pos + 1] : si[0];
             if (p.history) p.history[pos + 1] = next;
@@ -721,8 +737,9 @@ static cudaError_t dispatch_wk(const GemvParams& p, bool out_f32, int pro, int e
         return cudaErrorInvalidValue;
     }
     if (out_f32) {
-        if (pro != PRO_PLAIN) return cudaErrorInvalidValue;
-        return launch_one<WK, float, PRO_PLAIN, EPI_STORE>(p, s, pdl);
+        if (pro == PRO_PLAIN) return launch_one<WK, float, PRO_PLAIN, EPI_STORE>(p, s, pdl);
+        if (pro == PRO_ATTN_MERGE) return launch_one<WK, float, PRO_ATTN_MERGE, EPI_STORE>(p, s, pdl);
+        return cudaErrorInvalidValue;
     }
     switch (pro) {
         case PRO_PLAIN: return launch_one<WK, XT, PRO_PLAIN, EPI_STORE>(p, s, pdl);

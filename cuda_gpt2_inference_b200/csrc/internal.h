@@ -48,7 +48,8 @@ struct GemvParams {
     int aux_bytes = 0;            // shared memory for PRO_ATTN_MERGE partials
     // PRO_RES_LN / PRO_EMB_LN
     const void* res_in = nullptr;  // C, activation type
-    const void* delta = nullptr;   // C, activation type
+    const void* delta = nullptr;   // C, activation type (FP32 when delta_f32)
+    int delta_f32 = 0;             // delta is an FP32 all-reduced sum, rounded to the activation type on use
     void* res_out = nullptr;       // C, written by block 0
     void* ln_out = nullptr;        // C, written by block 0 (may be null)
     const void* ln_w = nullptr;
@@ -76,6 +77,8 @@ struct GemvParams {
     const int* prompt = nullptr;  // device prompt, n_prompt ints
     int n_prompt = 0;
     int advance = 1;              // 1: write next token and pos+1; 0: only the logits
+    float* pair_out = nullptr;    // tensor parallel: (best value, global index bits) instead of advancing
+    int row_offset = 0;           // global index of local row 0 (vocab shard)
 };
 
 // KV-cache storage kinds

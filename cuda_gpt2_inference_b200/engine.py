@@ -47,6 +47,23 @@ class Engine:
         return cls(h)
 
     @classmethod
+    def from_buffer_tp(cls, image: bytes, wmode: str, kvmode: str, scales: np.ndarray | None, tp_rank: int,
+                       tp_size: int, nccl_id: bytes) -> "Engine":
+        """This rank's engine of a tensor-parallel group (collective: every rank
+        calls it with the same image and 128-byte id, on its own device)."""
+        h = ctypes.c_void_p()
+        img = np.frombuffer(image, dtype=np.uint8)  # no copy: the library slices this rank's shard
+        sc_ptr, nsc = None, 0
+        if scales is not None:
+            scales = np.ascontiguousarray(scales, dtype=np.float32)
+            sc_ptr, nsc = scales.ctypes.data_as(ctypes.c_void_p), scales.size
+        uid = ctypes.create_string_buffer(bytes(nccl_id), 128)
+        check(lib().gpt2b_engine_create_tp_from_buffer(img.ctypes.data_as(ctypes.c_void_p), img.size, sc_ptr, nsc,
+                                                       WMODES[wmode], KVMODES[kvmode], int(tp_rank), int(tp_size),
+                                                       uid, ctypes.byref(h)), "gpt2b_engine_create_tp_from_buffer")
+        return cls(h)
+
+    @classmethod
     def from_file(cls, path: str, wmode: str = "bf16", kvmode: str = "floatx", scale_path: str | None = None):
         h = ctypes.c_void_p()
         check(lib().gpt2b_engine_create_from_file(path.encode(), scale_path.encode() if scale_path else None,

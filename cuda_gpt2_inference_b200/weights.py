@@ -89,6 +89,42 @@ def image(params: dict, cfg: dict, dtype: str) -> bytes:
     return b"".join(parts)
 
 
+def image_stream(cfg: dict, seed: int = 1234, init: str = "spec", dtype: str = "bf16") -> bytes:
+    """The bytes of ``image(synth_params(cfg, seed, init), cfg, dtype)`` built one
+    tensor at a time (peak host memory: the image plus one tensor), for
+    GPT-2-XL-sized models."""
+    if dtype not in ("f32", "bf16"):
+        raise ValueError(dtype)
+    eb = 4 if dtype == "f32" else 2
+    shp = shapes(cfg)
+    total = 1024 + sum(int(np.prod(v)) * eb for v in shp.values())
+    out = np.empty(total, np.uint8)
+    out[:1024] = np.frombuffer(header(cfg, 3 if dtype == "f32" else 5).tobytes(), np.uint8)
+    rng = np.random.default_rng(seed)
+    off = 1024
+    for name in NAMES:  # the synth_params draw order (dict order of shapes() == NAMES)
+        sh = shp[name]
+        if name in LINEAR:
+            a = rng.standard_normal(sh, dtype=np.float32) * np.float32(0.02)
+        elif name == "wpe":
+            a = rng.standard_normal(sh, dtype=np.float32) * np.float32(0.01)
+        elif name.endswith("w"):
+            a = np.ones(sh, np.float32)
+            if init == "test":
+                a += rng.standard_normal(sh, dtype=np.float32) * np.float32(0.1)
+        else:
+            a = np.zeros(sh, np.float32)
+            if init == "test":
+                a += rng.standard_normal(sh, dtype=np.float32) * np.float32(0.02)
+        if name == "wte":
+            a[cfg["V"]:] = 0.0
+        b = (np.ascontiguousarray(a) if dtype == "f32" else bf16_bits(a)).view(np.uint8).ravel()
+        out[off:off + b.size] = b
+        off += b.size
+        del a, b
+    return out.tobytes()
+
+
 def read_header(buf: bytes) -> tuple[int, dict]:
     h = np.frombuffer(buf[:1024], dtype=np.int32)
     if h[0] != MAGIC:

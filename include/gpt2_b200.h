@@ -315,6 +315,35 @@ int gpt2b_engine_set_position(gpt2b_engine* e, int token, int pos);
 /* Waits for the engine stream and copies history[first .. first+count) (the
  * token at each position; history[p+1] is the pick after position p) to host. */
 int gpt2b_engine_history(gpt2b_engine* e, int* out_host, int first, int count);
+/* ------------------------------------------------------------------------ */
+/* Tensor parallelism (no counterpart in the reference, which is single-GPU). */
+/* GPT-2-XL-style sharding for decode: QKV and FC column-parallel (this rank's */
+/* heads / FC rows), attention projection and FC projection row-parallel     */
+/* (FP32 partial sums all-reduced with NCCL), LM head vocab-parallel with an  */
+/* all-gather of (best logit, index) pairs; residual and LayerNorms replicated.*/
+/* Heads split unevenly (25 heads: 13/12, 7/6/6/6, 4/3x7); 4C and Vp must be  */
+/* divisible by 16*tp_size and tp_size.                                       */
+/* ------------------------------------------------------------------------ */
+/* 128-byte NCCL unique id for a new group (rank 0 creates it, the host       */
+/* distributes it).  GPT2B_ERR_UNSUPPORTED when built without NCCL.           */
+int gpt2b_nccl_unique_id(void* id_out);
+/* This rank's shard: out6 = {first head, heads, first FC row, FC rows, first */
+/* vocab row, vocab rows}.  Host only.                                        */
+int gpt2b_tp_plan(const gpt2b_config* cfg, int tp_rank, int tp_size, int* out6);
+/* This rank's parameter tensors (file order, element sizes as stored, sliced */
+/* per the plan; row-parallel biases only on rank 0, zeros elsewhere) and its */
+/* scale arrays.  With out_params NULL only the sizes are returned.  Host only.*/
+int gpt2b_tp_shard_image(const void* image, size_t nbytes, const float* scales, size_t nscales, int wmode,
+                         int tp_rank, int tp_size, void* out_params, size_t* out_bytes, float* out_scales,
+                         size_t* out_nscales);
+/* Collective over the tp_size ranks (one process per GPU, each on its own   */
+/* current device, all passing the same image and id): builds this rank's    */
+/* engine.  Its generate/decode/forward calls are collectives too; logits    */
+/* returned to the host are the full gathered Vp.  Per-kernel path only.     */
+int gpt2b_engine_create_tp_from_buffer(const void* image, size_t nbytes, const float* scales, size_t nscales,
+                                       int wmode, int kvmode, int tp_rank, int tp_size, const void* nccl_id,
+                                       gpt2b_engine** out);
+
 /* Kernel launches one step issues (for launch accounting); 0 when the
  * persistent kernel runs: it issues one launch per decode/generate call for
  * all of that call's steps. */
