@@ -457,7 +457,8 @@ def run_xl_tp(args, rank, local_rank, world):
                                 device_id=torch.device("cuda", local_rank))
     cfg, img, sc = xl_model(rank, world)
     if world > 1:
-        eng = tp.engine(img, "int8", "floatx", sc, rank, world, tp.shared_group_id(rank))
+        eng = tp.engine(img, "int8", "floatx", sc, rank, world, tp.shared_group_id(rank),
+                        p2p=(args.path == "persistent"))
     else:
         eng = Engine.from_buffer(img, "int8", "floatx", sc)
     del img
@@ -517,10 +518,11 @@ def run_xl_tp(args, rank, local_rank, world):
                 "d2h_bytes_per_step": (GEN + 1) * 4},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
-                     "kernel": "whole decode step per rank (%d kernels + %d NCCL collectives)" % (
-                         kps, 2 * cfg["L"] + 1 if world > 1 else 0),
+                     "kernel": ("whole decode step per rank (%d kernels + %d NCCL collectives)" % (
+                         kps, 2 * cfg["L"] + 1 if world > 1 else 0)) if kps else
+                               "persistent kernel per rank, peer stores between ranks (1 launch per %d steps)" % GEN,
                      "algorithmic_bytes_per_token": int(abytes)},
-        "gpu_launches": kps * GEN * args.steps,
+        "gpu_launches": kps * GEN * args.steps if kps else args.steps,
         "clocks": clk,
         "deterministic": bool(np.array_equal(decoded, e2e_tokens)),
     }

@@ -105,6 +105,8 @@ _SIGS = {
     "gpt2b_tp_plan": (_I, [_P, _I, _I, _P]),
     "gpt2b_tp_shard_image": (_I, [_P, _SZ, _P, _SZ, _I, _I, _I, _P, _P, _P, _P]),
     "gpt2b_engine_create_tp_from_buffer": (_I, [_P, _SZ, _P, _SZ, _I, _I, _I, _I, _P, _P]),
+    "gpt2b_engine_tp_ipc_handle": (_I, [_P, _P]),
+    "gpt2b_engine_tp_connect": (_I, [_P, _P, _I]),
 }
 
 _lib = None

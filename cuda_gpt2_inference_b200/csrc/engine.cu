@@ -89,6 +89,8 @@ struct gpt2b_engine {
     float* lm_pair = nullptr;      // (best logit, global index) of this rank's vocab rows
     float* lm_pairs = nullptr;     // every rank's pair
     float* logits_full = nullptr;  // all-gathered logits (Vp) for host copies and sampling
+    bool tp_connected = false;     // peers' exchange arenas mapped (persistent kernel usable)
+    unsigned char* peer_map[8] = {};  // IPC mappings of the other ranks' arenas
 #if GPT2B_HAVE_NCCL
     ncclComm_t comm = nullptr;
 #endif
@@ -249,6 +251,8 @@ void free_engine(gpt2b_engine* e) {
 #if GPT2B_HAVE_NCCL
     if (e->comm) ncclCommDestroy(e->comm);
 #endif
+    for (int r = 0; r < 8; r++)
+        if (e->peer_map[r]) cudaIpcCloseMemHandle(e->peer_map[r]);
     if (e->params) cudaFree(e->params);
     if (e->acts) cudaFree(e->acts);
     if (e->kv) cudaFree(e->kv);
@@ -394,45 +398,58 @@ __global__ void set_history_kernel(int* history, const int* d_token, const int* 
 // arena: tagged words per layer and phase, per-(layer, head) KV flags, the
 // epoch counter and the abort flag.
 cudaError_t setup_persistent(gpt2b_engine* e, int nsm) {
-    if (e->tp_size > 1) return cudaSuccess;  // tensor parallel: per-kernel path with collectives
     const gpt2b_config& c = e->cfg;
-    const int C = c.channels, NH = c.num_heads, L = c.num_layers, maxT = c.max_seq_len;
+    const int C = c.channels, L = c.num_layers, maxT = c.max_seq_len, TP = e->tp_size;
+    const int NHl = e->nh_l;  // this rank's heads
     int coop = 0;
     cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, e->device);
-    const int S = std::min(nsm / NH, persist_max_splits());
-    if (!coop || !persist_supported(C, NH, C / NH, maxT, S, nsm)) return cudaSuccess;
+    const int S = std::min(nsm / NHl, persist_max_splits());
+    if (!coop || TP > 8 || !persist_supported(C, NHl, 64, maxT, S, nsm)) return cudaSuccess;
+    const int kv_rows = engine_attn_chunk(maxT, S);
     int nsw = 0;
     for (int k = persist_max_stages(); k >= 2 && !nsw; k--) {
-        const int b = persist_smem_bytes(e->wk, e->kvk, C, k);
+        const int b = persist_smem_bytes(e->wk, e->kvk, C, k, kv_rows, TP);
         if (b > 0 && b <= max_dyn_smem()) nsw = k;
     }
     if (!nsw) return cudaSuccess;
     const int G = nsm;
-    const size_t n_qkv = (size_t)L * 3 * C, n_c = (size_t)L * C, n_fc = (size_t)L * 4 * C;
-    const size_t n_part = (size_t)L * NH * S * (64 + 2), n_lm = 2 * (size_t)G;
-    const size_t words = n_qkv + 3 * n_c + n_fc + n_part + n_lm;
-    const size_t flags = (size_t)L * NH;
-    size_t bytes = align256(words * 8) + align256(flags * 4) + 256;
+    const int Q = 3 * NHl * 64, A = NHl * 64, F = e->f_l;
+    // exchange arena: the cross-GPU parts first, at offsets every rank shares
+    // (abort flag, projection and FC-projection partials [L][TP][C], LM pairs
+    // [TP][G][2]), then this rank's own words and flags
+    const size_t n_grp = (size_t)L * TP * C, n_lm = 2 * (size_t)TP * G;
+    const size_t n_qkv = (size_t)L * Q, n_att = (size_t)L * A, n_fc = (size_t)L * F;
+    const size_t n_part = (size_t)L * NHl * S * (64 + 2);
+    const size_t off_proj = 256, off_fcproj = off_proj + n_grp * 8, off_lm = off_fcproj + n_grp * 8;
+    const size_t off_own = align256(off_lm + n_lm * 8);
+    const size_t own_words = n_qkv + n_att + n_part + n_fc;
+    const size_t off_flags = align256(off_own + own_words * 8);
+    const size_t flags = (size_t)L * NHl;
+    const size_t bytes = align256(off_flags + flags * 4) + 256;
     cudaError_t err = cudaMalloc(&e->xchg, bytes);
     if (err != cudaSuccess) return err;
     if ((err = cudaMemset(e->xchg, 0, bytes)) != cudaSuccess) return err;
     e->xchg_bytes = bytes;
     PersistParams& p = e->pp;
-    unsigned long long* w = reinterpret_cast<unsigned long long*>(e->xchg);
+    p.abort_flag = reinterpret_cast<int*>(e->xchg);
+    p.ll_proj = reinterpret_cast<unsigned long long*>(e->xchg + off_proj);
+    p.ll_fcproj = reinterpret_cast<unsigned long long*>(e->xchg + off_fcproj);
+    p.ll_lm = reinterpret_cast<unsigned long long*>(e->xchg + off_lm);
+    p.xoff_abort = 0; p.xoff_proj = off_proj; p.xoff_fcproj = off_fcproj; p.xoff_lm = off_lm;
+    unsigned long long* w = reinterpret_cast<unsigned long long*>(e->xchg + off_own);
     p.ll_qkv = w; w += n_qkv;
-    p.ll_atty = w; w += n_c;
+    p.ll_atty = w; w += n_att;
     p.ll_part = w; w += n_part;
-    p.ll_proj = w; w += n_c;
-    p.ll_fc = w; w += n_fc;
-    p.ll_fcproj = w; w += n_c;
-    p.ll_lm = w;
-    unsigned char* tail = e->xchg + align256(words * 8);
-    p.kv_flag = reinterpret_cast<unsigned*>(tail);
-    tail += align256(flags * 4);
-    p.d_epoch = reinterpret_cast<unsigned*>(tail);
-    p.abort_flag = reinterpret_cast<int*>(tail + 16);
-    p.C = C; p.L = L; p.NH = NH; p.V = c.vocab_size; p.Vp = c.padded_vocab_size; p.maxT = maxT;
-    p.splits = S; p.nsw = nsw; p.G = G;
+    p.ll_fc = w;
+    p.kv_flag = reinterpret_cast<unsigned*>(e->xchg + off_flags);
+    p.d_epoch = reinterpret_cast<unsigned*>(e->xchg + align256(off_flags + flags * 4));
+    for (int r = 0; r < 8; r++) p.peer_x[r] = nullptr;
+    p.peer_x[TP > 1 ? e->tp_rank : 0] = e->xchg;
+    p.tp_rank = TP > 1 ? e->tp_rank : 0;
+    p.tp_size = TP;
+    p.C = C; p.L = L; p.NH = NHl; p.V = c.vocab_size; p.Vp = c.padded_vocab_size; p.maxT = maxT;
+    p.splits = S; p.nsw = nsw; p.G = G; p.kv_rows = kv_rows;
+    p.qkv_rows = Q; p.proj_k = A; p.fc_rows = F; p.fcproj_k = F; p.v_rows = e->v_rows; p.v0 = e->v0;
     p.attn_scale = 1.0f / sqrtf(64.0f);
     p.W[0] = e->p[0]; p.W[1] = e->p[4]; p.W[2] = e->p[6]; p.W[3] = e->p[10]; p.W[4] = e->p[12];
     for (int g = 0; g < 5; g++) p.S[g] = e->sc[g];
@@ -444,8 +461,9 @@ cudaError_t setup_persistent(gpt2b_engine* e, int nsm) {
     p.kv_scale = e->kv_scale;
     p.d_token = e->d_token; p.d_pos = e->d_pos; p.history = e->d_history; p.prompt = e->d_prompt;
     p.logits = e->logits;
-    e->persist_ok = true;
-    e->use_persistent = true;
+    // single GPU: ready; tensor parallel: after gpt2b_engine_tp_connect maps the peers' arenas
+    e->persist_ok = (TP == 1);
+    e->use_persistent = (TP == 1);
     return cudaSuccess;
 }
 
@@ -775,6 +793,41 @@ int gpt2b_engine_create_tp_from_buffer(const void* image, size_t nbytes, const f
                         tp_size, nccl_id, out);
 }
 
+int gpt2b_engine_tp_ipc_handle(gpt2b_engine* e, void* handle_out) {
+    if (!e || !handle_out) return GPT2B_ERR_INVALID_ARG;
+    if (e->tp_size < 2 || !e->xchg) return GPT2B_ERR_UNSUPPORTED;
+    DeviceGuard g(e->device);
+    cudaIpcMemHandle_t h;
+    cudaError_t err = cudaIpcGetMemHandle(&h, e->xchg);
+    if (err != cudaSuccess) return status_from(err);
+    static_assert(sizeof(h) == 64, "IPC handle size");
+    memcpy(handle_out, &h, sizeof(h));
+    return GPT2B_OK;
+}
+
+int gpt2b_engine_tp_connect(gpt2b_engine* e, const void* handles, int n) {
+    if (!e || !handles) return GPT2B_ERR_INVALID_ARG;
+    if (e->tp_size < 2 || !e->xchg) return GPT2B_ERR_UNSUPPORTED;
+    if (n != e->tp_size) return GPT2B_ERR_INVALID_ARG;
+    if (e->tp_connected) return GPT2B_OK;
+    DeviceGuard g(e->device);
+    const unsigned char* hb = static_cast<const unsigned char*>(handles);
+    for (int r = 0; r < n; r++) {
+        if (r == e->tp_rank) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, hb + (size_t)r * 64, 64);
+        void* ptr = nullptr;
+        cudaError_t err = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+        if (err != cudaSuccess) return status_from(err);
+        e->peer_map[r] = static_cast<unsigned char*>(ptr);
+        e->pp.peer_x[r] = e->peer_map[r];
+    }
+    e->tp_connected = true;
+    e->persist_ok = true;
+    e->use_persistent = true;
+    return GPT2B_OK;
+}
+
 int gpt2b_nccl_unique_id(void* id_out) {
     if (!id_out) return GPT2B_ERR_INVALID_ARG;
 #if GPT2B_HAVE_NCCL
@@ -896,7 +949,7 @@ int gpt2b_engine_set_option(gpt2b_engine* e, int option, int value) {
             e->graphs_valid = false;
             break;
         case GPT2B_OPT_PERSISTENT:
-            if (value && !e->persist_ok) return GPT2B_ERR_UNSUPPORTED;
+            if (value && !e->persist_ok) return GPT2B_ERR_UNSUPPORTED;  // (tensor parallel: connect first)
             e->use_persistent = value != 0;
             break;
         default: return GPT2B_ERR_INVALID_ARG;

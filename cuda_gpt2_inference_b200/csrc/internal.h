@@ -97,6 +97,16 @@ int attn_engine_max_chunk(int kv);  // positions one engine CTA stages at once
 // one cooperative launch of G CTAs (one per SM).
 struct PersistParams {
     int C = 0, L = 0, NH = 0, V = 0, Vp = 0, maxT = 0, splits = 0, nsw = 0, G = 0;
+    int kv_rows = 0;  // positions one attention CTA stages (the largest chunk at maxT)
+    // this rank's matrix shapes (single GPU: 3C, C, 4C, 4C, Vp, 0) and tensor-parallel group;
+    // NH above is this rank's head count
+    int qkv_rows = 0, proj_k = 0, fc_rows = 0, fcproj_k = 0, v_rows = 0, v0 = 0;
+    int tp_rank = 0, tp_size = 1;
+    // exchange arena of every rank (own included; peers through IPC mappings) and the
+    // offsets of the cross-GPU parts: abort flag, projection / FC-projection partials
+    // [L][tp][C], LM pairs [tp][G][2]
+    unsigned char* peer_x[8] = {};
+    size_t xoff_abort = 0, xoff_proj = 0, xoff_fcproj = 0, xoff_lm = 0;
     float attn_scale = 0.125f;
     // parameters: layer-0 bases of the stacked tensors, storage per weight kind
     const unsigned char* W[5] = {};  // wte, qkvw, attprojw, fcw, fcprojw
@@ -107,7 +117,8 @@ struct PersistParams {
     // KV cache [layer][K|V][head][maxT][hs] and 8-bit scales [layer][K|V][head][maxT]
     unsigned char* kv = nullptr;
     float* kv_scale = nullptr;
-    // exchange words (step tag << 32 | float bits), zero-initialised
+    // exchange words (step tag << 32 | float bits), zero-initialised; ll_proj, ll_fcproj and
+    // ll_lm are this rank's copies of the cross-GPU parts
     unsigned long long *ll_qkv = nullptr, *ll_atty = nullptr, *ll_part = nullptr, *ll_proj = nullptr,
                        *ll_fc = nullptr, *ll_fcproj = nullptr, *ll_lm = nullptr;
     unsigned* kv_flag = nullptr;  // [layer][head]: last epoch whose KV append is complete
@@ -125,7 +136,7 @@ struct PersistParams {
 bool persist_supported(int C, int NH, int hs, int maxT, int splits, int nsm);
 int persist_max_splits();
 int persist_max_stages();
-int persist_smem_bytes(int wk, int kv, int C, int nsw);  // -1: unsupported kinds, or one CTA does not fit an SM
+int persist_smem_bytes(int wk, int kv, int C, int nsw, int kv_rows, int tp);  // -1: unsupported, or no fit
 cudaError_t launch_persistent(int wk, int kv, const PersistParams& P, cudaStream_t st);
 
 // per-translation-unit device error readers

@@ -36,7 +36,7 @@
 // Consumer warp w takes rows w and w + 8 of a stage (one row for K = 4C), two
 // independent dot products sharing each x chunk and one shuffle reduction.
 //
-// Shapes: head size 64, C <= 1024, heads x splits <= CTAs, at most 96
+// Shapes: head size 64, C <= 2048, heads x splits <= CTAs, at most 256
 // positions per attention CTA (persist_supported); the engine uses the
 // per-kernel path otherwise.
 #include "common.cuh"
@@ -57,11 +57,16 @@ constexpr int kStageUnits = 16;       // row-units of C elements per stage
 constexpr int kTailSlot = 96;         // a 16-byte aligned window of 16 bias (or scale) values
 constexpr int kTail = 2 * kTailSlot;  // stage tail: bias window + scale window
 constexpr int kMaxNs = 24;            // ring stages (upper bound)
-constexpr int kKvRows = 96;           // positions per attention CTA
+constexpr int kMaxKvRows = 256;       // positions per attention CTA (one per consumer thread in the softmax)
+constexpr int kMaxCtas = 160;         // CTAs of the grid (one per SM)
+constexpr int kMaxC = 2048;           // channels
+constexpr int kNarrowC = 1024;        // kernels for C <= 1024 keep per-thread arrays small
+constexpr int kNarrowKvRows = 96;     // and stage at most 96 positions per attention CTA
 constexpr int kHSz = 64;              // head size
 constexpr int kMaxSplits = 32;        // attention splits per head
 constexpr int kMiscFloats = 128;      // reduction scratch, new-row codes and scales, stop flag
-constexpr int kGatherJ = 16;          // exchange words per consumer thread and gather (4C <= 4096)
+constexpr int kGatherJ = 32;          // exchange words per consumer thread and gather (4C <= 8192)
+constexpr int kGatherJs = 16;         // the short gather (n <= 4096 words)
 constexpr uint32_t kPollLimit = 1u << 22;
 enum { kPhQkv = 0, kPhProj = 1, kPhFc = 2, kPhFcproj = 3, kPhLm = 4 };
 
@@ -69,7 +74,7 @@ enum { kPhQkv = 0, kPhProj = 1, kPhFc = 2, kPhFcproj = 3, kPhLm = 4 };
 // thread 0 of every CTA stamps %globaltimer at phase boundaries of the first
 // kTraceSteps steps.  Off in the library build.
 #ifdef GPT2B_PERSIST_TRACE
-constexpr int kTraceSteps = 4, kTraceCtas = 160, kTraceEv = 160;
+constexpr int kTraceSteps = 4, kTraceCtas = 160, kTraceEv = 640;
 __device__ unsigned long long g_trace[kTraceSteps * kTraceCtas * kTraceEv];
 #define PTRACE(ev)                                                                            \
     do {                                                                                      \
@@ -112,30 +117,55 @@ __device__ __forceinline__ unsigned long long ll_load(const unsigned long long* 
     asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
     return w;
 }
+// Words written by other GPUs of the group (system scope).
+__device__ __forceinline__ unsigned long long ll_load_sys(const unsigned long long* p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
 __device__ __forceinline__ bool aborted(const PersistParams& P) {
     return *(volatile const int*)P.abort_flag != 0;
+}
+__device__ __forceinline__ void ll_store_sys(unsigned long long* p, float v, uint32_t tag) {
+    const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+// A word of a cross-GPU part to every rank of the group (own copy included).
+template <bool TPG>
+__device__ __forceinline__ void ll_store_group(const PersistParams& P, size_t xoff, size_t word, float v,
+                                               uint32_t tag) {
+    if constexpr (!TPG) {
+        ll_store(reinterpret_cast<unsigned long long*>(P.peer_x[0] + xoff) + word, v, tag);
+    } else {
+        for (int r = 0; r < P.tp_size; r++)
+            ll_store_sys(reinterpret_cast<unsigned long long*>(P.peer_x[r] + xoff) + word, v, tag);
+    }
 }
 __device__ __noinline__ void give_up(const PersistParams& P) {
     report_device_error(GPT2B_DEVERR_GRID_TIMEOUT);
     atomicExch(P.abort_flag, 1);
+    for (int r = 0; r < P.tp_size; r++)  // the other ranks leave too
+        if (r != P.tp_rank)
+            asm volatile("st.relaxed.sys.global.b32 [%0], %1;" ::"l"(P.peer_x[r] + P.xoff_abort), "r"(1) : "memory");
 }
 
-// Words i = tid + j*kCT (i < n) of src into out[j]; all loads of a round are
-// in flight together.  False on timeout (recorded) or abort.
-__device__ __noinline__ bool ll_gather(const PersistParams& P, const unsigned long long* src, int n, uint32_t tag,
-                                       float* out) {
+// Words i = tid + j*kCT (i < n, j < J) of src into out[j]; all loads of a
+// round are in flight together.  False on timeout (recorded) or abort.
+template <int J, bool SYS>
+__device__ __noinline__ bool ll_gather_j(const PersistParams& P, const unsigned long long* src, int n, uint32_t tag,
+                                         float* out) {
     const int tid = threadIdx.x;
     uint32_t pending = 0;
 #pragma unroll
-    for (int j = 0; j < kGatherJ; j++)
+    for (int j = 0; j < J; j++)
         if (tid + j * kCT < n) pending |= 1u << j;
     for (uint32_t it = 0; pending; ++it) {
-        unsigned long long w[kGatherJ];
+        unsigned long long w[J];
 #pragma unroll
-        for (int j = 0; j < kGatherJ; j++)
-            if (pending & (1u << j)) w[j] = ll_load(src + tid + j * kCT);
+        for (int j = 0; j < J; j++)
+            if (pending & (1u << j)) w[j] = SYS ? ll_load_sys(src + tid + j * kCT) : ll_load(src + tid + j * kCT);
 #pragma unroll
-        for (int j = 0; j < kGatherJ; j++)
+        for (int j = 0; j < J; j++)
             if ((pending & (1u << j)) && (uint32_t)(w[j] >> 32) == tag) {
                 out[j] = __uint_as_float((uint32_t)w[j]);
                 pending &= ~(1u << j);
@@ -146,6 +176,18 @@ __device__ __noinline__ bool ll_gather(const PersistParams& P, const unsigned lo
         __nanosleep(32);
     }
     return true;
+}
+template <bool WIDE>
+__device__ __forceinline__ bool ll_gather(const PersistParams& P, const unsigned long long* src, int n, uint32_t tag,
+                                          float* out) {
+    if constexpr (!WIDE) return ll_gather_j<kGatherJs, false>(P, src, n, tag, out);
+    return n <= kGatherJs * kCT ? ll_gather_j<kGatherJs, false>(P, src, n, tag, out)
+                                : ll_gather_j<kGatherJ, false>(P, src, n, tag, out);
+}
+// Words written by the ranks of a tensor-parallel group (system scope, 32-word rounds).
+__device__ __forceinline__ bool ll_gather_group(const PersistParams& P, const unsigned long long* src, int n,
+                                                uint32_t tag, float* out) {
+    return ll_gather_j<kGatherJ, true>(P, src, n, tag, out);
 }
 
 // consumer-only barriers (named barrier 1, the 256 consumer threads)
@@ -198,17 +240,25 @@ template <> struct PTraits<WK_BF16> { using XT = __nv_bfloat16; static constexpr
 template <> struct PTraits<WK_I8> { using XT = __nv_bfloat16; static constexpr int kWB = 1; };
 template <> struct PTraits<WK_FP8> { using XT = __nv_bfloat16; static constexpr int kWB = 1; };
 
-// Rows, stage geometry and this CTA's row range of phase `ph`: K = C phases
-// take 16 rows per stage, FCPROJ (K = 4C) 8 rows per stage in two K-halves.
+// Rows, columns, stage geometry and this CTA's row range of phase `ph` (this
+// rank's shard): K <= C takes 16 rows per stage; wider rows (FCPROJ, K = 4C /
+// tp) 8 rows per stage, in K-parts of at most 2C.
 struct PhaseRows {
-    int M, kparts, rs, c0, c1;  // rows, K-parts per row, rows per stage, CTA range
+    int M, K, kparts, part, rs, c0, c1;  // rows, columns, K-parts, columns per part, rows per stage, CTA range
 };
 __device__ __forceinline__ PhaseRows phase_rows(const PersistParams& P, int ph, int b) {
     PhaseRows r;
     const int C = P.C;
-    r.M = (ph == kPhQkv) ? 3 * C : (ph == kPhFc) ? 4 * C : (ph == kPhLm) ? P.Vp : C;
-    r.kparts = (ph == kPhFcproj) ? 2 : 1;
-    r.rs = (ph == kPhFcproj) ? kStageUnits / 2 : kStageUnits;
+    r.M = (ph == kPhQkv) ? P.qkv_rows : (ph == kPhFc) ? P.fc_rows : (ph == kPhLm) ? P.v_rows : C;
+    r.K = (ph == kPhProj) ? P.proj_k : (ph == kPhFcproj) ? P.fcproj_k : C;
+    if (r.K <= C) {
+        r.rs = kStageUnits;
+        r.kparts = 1;
+    } else {
+        r.rs = kStageUnits / 2;
+        r.kparts = (r.K + 2 * C - 1) / (2 * C);
+    }
+    r.part = r.K / r.kparts;
     r.c0 = b * r.M / P.G;
     r.c1 = (b + 1) * r.M / P.G;
     return r;
@@ -315,11 +365,11 @@ __device__ __forceinline__ uint8_t kv_encode(float x, float scale) {
 // shared memory layout
 // ---------------------------------------------------------------------------
 struct PSmem {
-    int stage_bytes, ring, kvbuf, uni, res, misc, bars, total;
+    int stage_bytes, ring, kvbuf, uni, res, lnp, red, misc, bars, total;
 };
 
 template <int WK, int KV>
-__host__ __device__ inline PSmem persist_layout(int C, int ns) {
+__host__ __device__ inline PSmem persist_layout(int C, int ns, int kv_rows, int tp) {
     const int xb = (WK == WK_F32) ? 4 : 2;
     const int wb = PTraits<WK>::kWB;
     const int kvb = (KV == KV_F32) ? 4 : (KV == KV_BF16 ? 2 : 1);
@@ -329,15 +379,18 @@ __host__ __device__ inline PSmem persist_layout(int C, int ns) {
     s.stage_bytes = kStageUnits * C * wb + kTail;
     int off = 0;
     s.ring = off; off += ns * s.stage_bytes;
-    s.kvbuf = off; off += 2 * kKvRows * kHSz * kvb + (k8 ? 2 * (kKvRows + 8) * 4 : 0);
+    s.kvbuf = off; off += 2 * kv_rows * kHSz * kvb + (k8 ? 2 * (kv_rows + 8) * 4 : 0);
     off = (off + 15) & ~15;
     s.uni = off;  // x vector of the current phase, or the attention scratch
-    const int xs_bytes = 4 * C * xb;
-    const int attn_bytes = (rpp * kHSz + 3 * kHSz + kKvRows + (kMaxSplits - 1) * (kHSz + 2)) * 4;
+    int xs_bytes = 4 * C * xb;
+    if (tp * kMaxCtas * 8 > xs_bytes) xs_bytes = tp * kMaxCtas * 8;  // the LM pairs of every CTA of every rank
+    const int attn_bytes = (rpp * kHSz + 3 * kHSz + kv_rows + (kMaxSplits - 1) * (kHSz + 2)) * 4;
     off += ((xs_bytes > attn_bytes ? xs_bytes : attn_bytes) + 15) & ~15;
     s.res = off; off += C * 4;
+    s.lnp = off; off += ((2 * C * xb) + 15) & ~15;  // LayerNorm gamma | beta of the current phase
+    s.red = off; off += (tp > 1) ? tp * C * 4 : 0;  // every rank's projection partials
     s.misc = off; off += kMiscFloats * 4;
-    s.bars = off; off += (2 * kMaxNs + 2) * 8;
+    s.bars = off; off += (2 * kMaxNs + 3) * 8;
     s.total = off;
     return s;
 }
@@ -345,8 +398,14 @@ __host__ __device__ inline PSmem persist_layout(int C, int ns) {
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <int WK, int KV>
+// MODE 0 (narrow): C <= 1024, at most 96 positions per attention CTA,
+// LayerNorm parameters in registers, short gathers.  MODE 1 (wide): C up to
+// 2048 and attention chunks up to 256 positions (GPT-2-XL).  MODE 2: wide,
+// as one rank of a tensor-parallel group.
+template <int WK, int KV, int MODE>
 __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const PersistParams P) {
+    constexpr bool WIDE = MODE >= 1;
+    constexpr bool TPG = MODE == 2;
     using XT = typename PTraits<WK>::XT;
     constexpr int kWB = PTraits<WK>::kWB;
     constexpr int kXB = (int)sizeof(XT);
@@ -359,17 +418,22 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
     constexpr int kE = 16 / kvb;       // elements per 16-byte slice
     using KT = typename PTraits<(KV == KV_F32) ? WK_F32 : WK_BF16>::XT;  // KV element type (float kinds)
     extern __shared__ __align__(16) unsigned char sm[];
-    const PSmem lay = persist_layout<WK, KV>(P.C, P.nsw);
+    const PSmem lay = persist_layout<WK, KV>(P.C, P.nsw, WIDE ? P.kv_rows : kNarrowKvRows, P.tp_size);
+    const int kKvRows = WIDE ? P.kv_rows : kNarrowKvRows;  // staged positions per attention CTA
+    constexpr int kCPT = (WIDE ? kMaxC : kNarrowC) / kCT;  // channels per consumer thread
     unsigned char* ring = sm + lay.ring;
     unsigned char* kvbuf = sm + lay.kvbuf;
     unsigned char* xs = sm + lay.uni;
     float* res = reinterpret_cast<float*>(sm + lay.res);
+    float* red = reinterpret_cast<float*>(sm + lay.red);
     float* misc = reinterpret_cast<float*>(sm + lay.misc);
     int* misc_i = reinterpret_cast<int*>(misc);
     volatile int* stop = misc_i + (kMiscFloats - 1);  // consumers left early: the producer stops
     uint64_t* full = reinterpret_cast<uint64_t*>(sm + lay.bars);
     uint64_t* empty = full + kMaxNs;
     uint64_t* kv_bar = empty + kMaxNs;
+    uint64_t* ln_bar = kv_bar + 1;
+    const XT* lnp = reinterpret_cast<const XT*>(sm + lay.lnp);
     // attention scratch (aliases xs: never live at the same time)
     float* accbuf = reinterpret_cast<float*>(xs);
     float* q_s = accbuf + kRPP * kHSz;
@@ -402,6 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
             mbar_init(&empty[i], kCW);
         }
         mbar_init(kv_bar, 1);
+        mbar_init(ln_bar, 1);
         *stop = 0;
         mbar_fence_init();
     }
@@ -419,16 +484,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                 const int ph = (u == 4 * L) ? kPhLm : (u & 3);
                 const PhaseRows pr = phase_rows(P, ph, b);
                 const int widx = phase_widx(ph);
-                const int part_bytes = (kStageUnits / pr.rs) * unit_bytes;  // per row and stage
-                const size_t row_bytes = (size_t)pr.kparts * part_bytes;
-                const unsigned char* wl = P.W[widx] + (size_t)l * pr.M * row_bytes;
+                const int part_bytes = pr.part * kWB;  // per row and stage
+                const size_t row_bytes = (size_t)pr.K * kWB;
+                const unsigned char* wl = P.W[widx] + (ph == kPhLm ? (size_t)P.v0 * row_bytes
+                                                                   : (size_t)l * pr.M * row_bytes);
                 const unsigned char* bias = nullptr;
                 if (ph == kPhQkv) bias = reinterpret_cast<const unsigned char*>(P.qkvb);
                 else if (ph == kPhProj) bias = reinterpret_cast<const unsigned char*>(P.attprojb);
                 else if (ph == kPhFc) bias = reinterpret_cast<const unsigned char*>(P.fcb);
                 else if (ph == kPhFcproj) bias = reinterpret_cast<const unsigned char*>(P.fcprojb);
                 if (bias) bias += (size_t)l * pr.M * kXB;
-                const float* scl = w8 ? P.S[widx] + (ph == kPhLm ? 0 : (size_t)l * pr.M) : nullptr;
+                const float* scl = w8 ? P.S[widx] + (ph == kPhLm ? (size_t)P.v0 : (size_t)l * pr.M) : nullptr;
                 for (int r0 = pr.c0; r0 < pr.c1; r0 += pr.rs) {
                     const int nr = min(pr.rs, pr.c1 - r0);
                     for (int kq = 0; kq < pr.kparts; kq++) {
@@ -490,6 +556,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
     int cst = 0;            // ring position of the next stage
     uint32_t cpar = 0;      // and its full-barrier parity
     int kv_issued = 0, kv_uses = 0;
+    uint32_t ln_par = 0;    // phase parity of the LayerNorm parameter barrier
+    bool ln_pending = false;  // thread 0: a parameter copy is in flight
 #ifdef GPT2B_PERSIST_TRACE
     int consumed_n = 0;
 #endif
@@ -543,7 +611,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
 
     {
         const XT* wpe = reinterpret_cast<const XT*>(P.wpe);
-        float gv[kGatherJ];
+        float gv[(WIDE || TPG) ? kGatherJ : kGatherJs];
         for (int step = 0; step < P.n_steps; step++) {
             const uint32_t tag = epoch0 + (uint32_t)step + 1u;
             const int pos = pos0 + step;
@@ -559,20 +627,33 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
 
                 // ---------- x of this phase ----------
                 if (ph == kPhQkv || ph == kPhFc || lm) {
-                    // residual update (fcproj of the previous layer, or proj), then LayerNorm
-                    const void* lnw = lm ? P.lnfw : (ph == kPhQkv ? P.ln1w : P.ln2w);
-                    const void* lnb = lm ? P.lnfb : (ph == kPhQkv ? P.ln1b : P.ln2b);
-                    const size_t lo = lm ? 0 : (size_t)l * C;
-                    float lw[4], lb[4];  // parameters loaded before the wait
+                    // residual update (fcproj of the previous layer, or proj), then LayerNorm;
+                    // gamma and beta are loaded (narrow: into registers; wide: bulk-copied into
+                    // shared memory) while the inputs are awaited
+                    float lw[WIDE ? 1 : kCPT], lb[WIDE ? 1 : kCPT];
+                    if constexpr (!WIDE) {
+                        const XT* lnw = reinterpret_cast<const XT*>(lm ? P.lnfw : (ph == kPhQkv ? P.ln1w : P.ln2w));
+                        const XT* lnb = reinterpret_cast<const XT*>(lm ? P.lnfb : (ph == kPhQkv ? P.ln1b : P.ln2b));
+                        const size_t lo = lm ? 0 : (size_t)l * C;
 #pragma unroll
-                    for (int j = 0; j < 4; j++) {
-                        const int c = tid + j * kCT;
-                        lw[j] = c < C ? to_f<XT>(reinterpret_cast<const XT*>(lnw)[lo + c]) : 0.0f;
-                        lb[j] = c < C ? to_f<XT>(reinterpret_cast<const XT*>(lnb)[lo + c]) : 0.0f;
+                        for (int j = 0; j < kCPT; j++) {
+                            const int c = tid + j * kCT;
+                            lw[j] = c < C ? to_f<XT>(lnw[lo + c]) : 0.0f;
+                            lb[j] = c < C ? to_f<XT>(lnb[lo + c]) : 0.0f;
+                        }
+                    } else if (tid == 0) {
+                        const void* lnw = lm ? P.lnfw : (ph == kPhQkv ? P.ln1w : P.ln2w);
+                        const void* lnb = lm ? P.lnfb : (ph == kPhQkv ? P.ln1b : P.ln2b);
+                        const size_t lo = lm ? 0 : (size_t)l * C;
+                        const uint32_t nb = (uint32_t)(C * sizeof(XT));
+                        mbar_arrive_expect_tx(ln_bar, 2 * nb);
+                        bulk_g2s(sm + lay.lnp, reinterpret_cast<const XT*>(lnw) + lo, nb, ln_bar);
+                        bulk_g2s(sm + lay.lnp + nb, reinterpret_cast<const XT*>(lnb) + lo, nb, ln_bar);
+                        ln_pending = true;
                     }
                     if (u == 0) {  // embedding: res = round(wte[tok] + wpe[pos]) (encoder_forward_kv)
-#pragma unroll
-                        for (int j = 0; j < 4; j++) {
+#pragma unroll 1
+                        for (int j = 0; j < kCPT; j++) {
                             const int c = tid + j * kCT;
                             if (c < C) {
                                 float e;
@@ -587,13 +668,37 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                             }
                         }
                     } else {
-                        const unsigned long long* src =
-                            (ph == kPhFc) ? P.ll_proj + (size_t)l * C : P.ll_fcproj + (size_t)(lm ? L - 1 : l - 1) * C;
-                        const bool ok = ll_gather(P, src, C, tag, gv);
+                        const int TP = TPG ? P.tp_size : 1;
+                        const size_t lsrc = (ph == kPhFc) ? (size_t)l : (size_t)(lm ? L - 1 : l - 1);
+                        const unsigned long long* src = ((ph == kPhFc) ? P.ll_proj : P.ll_fcproj) + lsrc * TP * C;
+                        bool ok = true;
+                        if constexpr (!TPG) {
+                            ok = ll_gather<WIDE>(P, src, C, tag, gv);
 #pragma unroll
-                        for (int j = 0; j < 4; j++) {
-                            const int c = tid + j * kCT;
-                            if (c < C) res[c] = round_to<XT>(res[c] + gv[j]);
+                            for (int j = 0; j < kCPT; j++) {
+                                const int c = tid + j * kCT;
+                                if (c < C) res[c] = round_to<XT>(res[c] + gv[j]);
+                            }
+                        } else {
+                            // every rank's FP32 partial [TP][C] into red, then the sum in rank
+                            // order (the same on every rank), rounded as the single-GPU store
+                            const int n = TP * C;
+                            for (int base = 0; base < n && ok; base += kGatherJ * kCT) {
+                                ok = ll_gather_group(P, src + base, min(n - base, kGatherJ * kCT), tag, gv);
+#pragma unroll
+                                for (int j = 0; j < kGatherJ; j++)
+                                    if (base + tid + j * kCT < n) red[base + tid + j * kCT] = gv[j];
+                            }
+                            cta_sync();
+#pragma unroll
+                            for (int j = 0; j < kCPT; j++) {
+                                const int c = tid + j * kCT;
+                                if (c < C) {
+                                    float v = 0.0f;
+                                    for (int r = 0; r < TP; r++) v += red[r * C + c];
+                                    res[c] = round_to<XT>(res[c] + round_to<XT>(v));
+                                }
+                            }
                         }
                         if (cta_any(!ok)) goto consumer_abort;
                     }
@@ -601,7 +706,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                     // residual; warp totals in misc[0..7] then misc[8..15], one barrier each
                     float s = 0.0f;
 #pragma unroll
-                    for (int j = 0; j < 4; j++) if (tid + j * kCT < C) s += res[tid + j * kCT];
+                    for (int j = 0; j < kCPT; j++) if (tid + j * kCT < C) s += res[tid + j * kCT];
                     s = warp_sum(s);
                     if (lane == 0) misc[warp] = s;
                     cta_sync();
@@ -611,7 +716,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                     const float mean = s / (float)C;
                     float q = 0.0f;
 #pragma unroll
-                    for (int j = 0; j < 4; j++)
+                    for (int j = 0; j < kCPT; j++)
                         if (tid + j * kCT < C) { const float d = res[tid + j * kCT] - mean; q += d * d; }
                     q = warp_sum(q);
                     if (lane == 0) misc[kCW + warp] = q;
@@ -620,19 +725,27 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
 #pragma unroll
                     for (int w = 0; w < kCW; w++) q += misc[kCW + w];
                     const float rstd = rsqrtf(q / (float)C + 1e-5f);
+                    if constexpr (WIDE) {
+                        if (!mbar_wait(ln_bar, ln_par)) bad = true;
+                        ln_par ^= 1u;
+                        ln_pending = false;
+                    }
 #pragma unroll
-                    for (int j = 0; j < 4; j++) {
+                    for (int j = 0; j < kCPT; j++) {
                         const int c = tid + j * kCT;
-                        if (c < C) xv[c] = from_f<XT>((rstd * (res[c] - mean)) * lw[j] + lb[j]);
+                        if (c < C) {
+                            const float g = WIDE ? to_f<XT>(lnp[c]) : lw[j];
+                            const float bb = WIDE ? to_f<XT>(lnp[C + c]) : lb[j];
+                            xv[c] = from_f<XT>((rstd * (res[c] - mean)) * g + bb);
+                        }
                     }
                 } else {
-                    // PROJ: x = atty of this layer; FCPROJ: x = gelu(fc) of this layer
-                    const int n = (ph == kPhProj) ? C : 4 * C;
-                    const unsigned long long* src =
-                        (ph == kPhProj) ? P.ll_atty + (size_t)l * C : P.ll_fc + (size_t)l * 4 * C;
-                    const bool ok = ll_gather(P, src, n, tag, gv);
+                    // PROJ: x = atty of this rank's heads; FCPROJ: x = gelu(fc) of this rank's FC rows
+                    const int n = (ph == kPhProj) ? P.proj_k : P.fcproj_k;
+                    const unsigned long long* src = (ph == kPhProj) ? P.ll_atty + (size_t)l * n : P.ll_fc + (size_t)l * n;
+                    const bool ok = ll_gather<WIDE>(P, src, n, tag, gv);
 #pragma unroll
-                    for (int j = 0; j < kGatherJ; j++)
+                    for (int j = 0; j < (WIDE ? kGatherJ : kGatherJs); j++)
                         if (tid + j * kCT < n) xv[tid + j * kCT] = from_f<XT>(gv[j]);
                     if (cta_any(!ok)) goto consumer_abort;
                 }
@@ -648,7 +761,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                     else if (ph == kPhFc) out = P.ll_fc + (size_t)l * pr.M;
                     else if (ph == kPhFcproj) out = P.ll_fcproj + (size_t)l * pr.M;
                     const bool has_bias = !lm;
-                    const int part_bytes = (kStageUnits / pr.rs) * unit_bytes;
+                    const int part_bytes = pr.part * kWB;
                     const int pc = part_bytes / 16;                   // chunks per row and stage
                     const bool two = (pr.rs == kStageUnits);         // rows warp and warp + 8
                     for (int r0 = pr.c0; r0 < pr.c1; r0 += pr.rs) {
@@ -702,7 +815,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                                     if (has_bias) v += to_f<XT>(bw[rl]);
                                     if (lm) {
                                         P.logits[row] = v;
-                                        if (row < P.V) best_merge(best_v, best_i, v, row);
+                                        if (P.v0 + row < P.V) best_merge(best_v, best_i, v, P.v0 + row);
+                                    } else if (ph == kPhProj || ph == kPhFcproj) {  // partials to every rank
+                                        ll_store_group<TPG>(P, ph == kPhProj ? P.xoff_proj : P.xoff_fcproj,
+                                                            ((size_t)l * (TPG ? P.tp_size : 1) + P.tp_rank) * C + row,
+                                                            TPG ? v : round_to<XT>(v), tag);
                                     } else {
                                         ll_store(out + row, round_to<XT>(ph == kPhFc ? gelu_tanh(v) : v), tag);
                                     }
@@ -723,14 +840,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
 
                 // ---------- after QKV: attention (head ah, split as) ----------
                 if (ph == kPhQkv && attn_cta) {
-                    const unsigned long long* qkv_w = P.ll_qkv + (size_t)l * 3 * C;
+                    const unsigned long long* qkv_w = P.ll_qkv + (size_t)l * P.qkv_rows;
                     const int total = pos + 1;
                     const int chunk = engine_attn_chunk(total, S);
                     const int j0 = as * chunk, j1 = min(j0 + chunk, total);
                     const int n_local = j1 - j0;
                     const int s_eff = min(S, (total + chunk - 1) / chunk);
                     if (tid < 3 * kHSz) {
-                        const unsigned long long* src = qkv_w + (size_t)(tid >> 6) * C + (size_t)ah * kHSz + (tid & 63);
+                        const unsigned long long* src =
+                            qkv_w + (size_t)(tid >> 6) * (NH * kHSz) + (size_t)ah * kHSz + (tid & 63);
                         float v = 0.0f;
                         for (uint32_t it = 0;; ++it) {
                             const unsigned long long w = ll_load(src);
@@ -890,7 +1008,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                     } else {
                         // split 0 merges the head's partials and publishes atty
                         const int nw = (s_eff - 1) * (kHSz + 2);  // <= 31 * 66 <= 8 * kCT
-                        if (!ll_gather(P, part + (kHSz + 2), nw, tag, gv)) bad = true;
+                        if (!ll_gather<WIDE>(P, part + (kHSz + 2), nw, tag, gv)) bad = true;
 #pragma unroll
                         for (int j = 0; j < 8; j++)
                             if (tid + j * kCT < nw) mrg[tid + j * kCT] = gv[j];
@@ -905,7 +1023,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                                 of += rs * mrg[k * (kHSz + 2) + tid];
                                 lf += rs * mrg[k * (kHSz + 2) + kHSz + 1];
                             }
-                            ll_store(P.ll_atty + (size_t)l * C + (size_t)ah * kHSz + tid, round_to<XT>(of / lf), tag);
+                            ll_store(P.ll_atty + (size_t)l * P.proj_k + (size_t)ah * kHSz + tid, round_to<XT>(of / lf), tag);
                         }
                     }
                     if (cta_any(bad)) goto consumer_abort;  // also carries a failed kv_issue
@@ -921,21 +1039,24 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
             }
             if (lane == 0) { misc[warp] = best_v; misc_i[16 + warp] = best_i; }
             cta_sync();
+            const int NG = (TPG ? P.tp_size : 1) * G;  // (value, index) pairs of every CTA of every rank
             if (tid == 0) {
                 float bv = misc[0];
                 int bi = misc_i[16];
                 for (int w = 1; w < kCW; w++) best_merge(bv, bi, misc[w], misc_i[16 + w]);
-                ll_store(P.ll_lm + 2 * b, bv, tag);
-                ll_store(P.ll_lm + 2 * b + 1, __int_as_float(bi), tag);
+                const size_t word = 2 * ((size_t)P.tp_rank * G + b);
+                ll_store_group<TPG>(P, P.xoff_lm, word, bv, tag);
+                ll_store_group<TPG>(P, P.xoff_lm, word + 1, __int_as_float(bi), tag);
             }
             {
-                const bool ok = ll_gather(P, P.ll_lm, 2 * G, tag, gv);
+                const bool ok = TPG ? ll_gather_group(P, P.ll_lm, 2 * NG, tag, gv)
+                                    : ll_gather<WIDE>(P, P.ll_lm, 2 * G, tag, gv);
                 float* gvals = reinterpret_cast<float*>(xs);
-                int* gidx = reinterpret_cast<int*>(xs) + G;
+                int* gidx = reinterpret_cast<int*>(xs) + NG;
 #pragma unroll
-                for (int j = 0; j < 2; j++) {
+                for (int j = 0; j < (TPG ? kGatherJ : 2); j++) {
                     const int wi = tid + j * kCT;
-                    if (wi < 2 * G) {
+                    if (wi < 2 * NG) {
                         if (wi & 1) gidx[wi >> 1] = __float_as_int(gv[j]);
                         else gvals[wi >> 1] = gv[j];
                     }
@@ -944,7 +1065,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                 PTRACE(4 * L * 3 + 2);
                 float bv = -FLT_MAX;
                 int bi = 0x7fffffff;
-                for (int k = tid; k < G; k += kCT) best_merge(bv, bi, gvals[k], gidx[k]);
+                for (int k = tid; k < NG; k += kCT) best_merge(bv, bi, gvals[k], gidx[k]);
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) {
                     const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
@@ -981,15 +1102,17 @@ consumer_abort:
     if (tid == 0) *stop = 1;  // the producer stops issuing and drains
 consumer_exit:
     if (tid == 0 && kv_issued > kv_uses) mbar_wait(kv_bar, (uint32_t)(kv_uses & 1));
+    if (tid == 0 && ln_pending) mbar_wait(ln_bar, ln_par);
 }
 
 // smem_out != null: report the shared memory of a launch with P.C, P.nsw and
 // whether one CTA of it fits on an SM (-1 if not); no launch.
-template <int WK, int KV>
+template <int WK, int KV, int MODE>
 cudaError_t launch_persist_t(const PersistParams& P, cudaStream_t st, int* smem_out) {
-    auto k = decode_persistent_kernel<WK, KV>;
+    constexpr bool WIDE = MODE >= 1;
+    auto k = decode_persistent_kernel<WK, KV, MODE>;
     static unsigned long long smem_set = 0;
-    const PSmem lay = persist_layout<WK, KV>(P.C, P.nsw);
+    const PSmem lay = persist_layout<WK, KV>(P.C, P.nsw, WIDE ? P.kv_rows : kNarrowKvRows, P.tp_size);
     cudaError_t e = ensure_smem_limit(k, &smem_set);
     if (e != cudaSuccess) return e;
     if (smem_out) {
@@ -1012,8 +1135,11 @@ cudaError_t launch_persist_t(const PersistParams& P, cudaStream_t st, int* smem_
 }
 
 cudaError_t persist_dispatch(int wk, int kv, const PersistParams& P, cudaStream_t st, int* smem_out) {
+    const int mode = P.tp_size > 1 ? 2 : ((P.C <= kNarrowC && P.kv_rows <= kNarrowKvRows) ? 0 : 1);
 #define GPT2B_PK(W_, K_) \
-    if (wk == W_ && kv == K_) return launch_persist_t<W_, K_>(P, st, smem_out);
+    if (wk == W_ && kv == K_)                                                   \
+        return mode == 0 ? launch_persist_t<W_, K_, 0>(P, st, smem_out)       \
+                         : (mode == 1 ? launch_persist_t<W_, K_, 1>(P, st, smem_out) : launch_persist_t<W_, K_, 2>(P, st, smem_out));
     GPT2B_PK(WK_F32, KV_F32)
     GPT2B_PK(WK_BF16, KV_BF16)
     GPT2B_PK(WK_I8, KV_BF16)
@@ -1036,19 +1162,21 @@ extern "C" int gpt2b_persist_trace_stages(unsigned long long* host) {
 }
 #endif
 
-int persist_smem_bytes(int wk, int kv, int C, int nsw) {
+int persist_smem_bytes(int wk, int kv, int C, int nsw, int kv_rows, int tp) {
     PersistParams P;
     P.C = C;
     P.nsw = nsw;
+    P.kv_rows = kv_rows;
+    P.tp_size = tp;
     int s = -1;
     if (persist_dispatch(wk, kv, P, nullptr, &s) != cudaSuccess) return -1;
     return s;
 }
 
 bool persist_supported(int C, int NH, int hs, int maxT, int splits, int nsm) {
-    if (hs != kHSz || C > 1024 || C % 64 != 0 || (NH * maxT) % 4 != 0) return false;
+    if (hs != kHSz || C > kMaxC || C % 64 != 0 || (NH * maxT) % 4 != 0 || nsm > kMaxCtas) return false;
     if (splits < 1 || splits > kMaxSplits || NH * splits > nsm) return false;
-    return engine_attn_chunk(maxT, splits) <= kKvRows;
+    return engine_attn_chunk(maxT, splits) <= kMaxKvRows;
 }
 
 int persist_max_splits() { return kMaxSplits; }

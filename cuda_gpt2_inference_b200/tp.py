@@ -60,7 +60,38 @@ def shared_group_id(rank: int) -> bytes:
     return obj[0]
 
 
-def engine(image: bytes, wmode: str, kvmode: str, scales, rank: int, size: int, group_id: bytes):
-    """This rank's engine (collective over the group)."""
+def all_gather_bytes(data: bytes) -> list:
+    """Every rank's ``data`` in rank order, through the default
+    ``torch.distributed`` process group."""
+    import torch.distributed as dist
+    out = [None] * dist.get_world_size()
+    dist.all_gather_object(out, data)
+    return out
+
+
+def connect(eng, exchange=all_gather_bytes) -> None:
+    """Map every rank's exchange arena into this rank's engine (collective):
+    the persistent kernel then runs the group's decode with peer stores over
+    NVLink instead of NCCL calls.  ``exchange(bytes) -> list[bytes]`` gathers
+    one value per rank in rank order."""
+    h = ctypes.create_string_buffer(64)
+    check(lib().gpt2b_engine_tp_ipc_handle(eng._h, h), "gpt2b_engine_tp_ipc_handle")
+    handles = exchange(h.raw)
+    buf = ctypes.create_string_buffer(b"".join(handles), 64 * len(handles))
+    check(lib().gpt2b_engine_tp_connect(eng._h, buf, len(handles)), "gpt2b_engine_tp_connect")
+
+
+def engine(image: bytes, wmode: str, kvmode: str, scales, rank: int, size: int, group_id: bytes,
+           p2p: bool = True, exchange=all_gather_bytes):
+    """This rank's engine (collective over the group).  With ``p2p`` the ranks'
+    exchange arenas are mapped into each other (:func:`connect`) and decoding
+    runs in the persistent kernel; otherwise the per-kernel path with NCCL."""
     from .engine import Engine
-    return Engine.from_buffer_tp(image, wmode, kvmode, scales, rank, size, group_id)
+    eng = Engine.from_buffer_tp(image, wmode, kvmode, scales, rank, size, group_id)
+    if p2p and size > 1:
+        try:
+            connect(eng, exchange)
+        except Exception:
+            eng.close()
+            raise
+    return eng

@@ -344,6 +344,14 @@ int gpt2b_engine_create_tp_from_buffer(const void* image, size_t nbytes, const f
                                        int wmode, int kvmode, int tp_rank, int tp_size, const void* nccl_id,
                                        gpt2b_engine** out);
 
+/* Persistent kernel across the group: the row-parallel partial sums and the  */
+/* LM-head picks go straight into every rank's exchange arena (peer stores   */
+/* over NVLink, tagged words, no NCCL).  Each rank exports the IPC handle of */
+/* its arena (64 bytes); the host gathers the tp_size handles in rank order  */
+/* and every rank connects; the engine then uses the persistent kernel.      */
+int gpt2b_engine_tp_ipc_handle(gpt2b_engine* e, void* handle_out);
+int gpt2b_engine_tp_connect(gpt2b_engine* e, const void* handles, int n);
+
 /* Kernel launches one step issues (for launch accounting); 0 when the
  * persistent kernel runs: it issues one launch per decode/generate call for
  * all of that call's steps. */

@@ -168,6 +168,31 @@ def test_long_context_matches_oracle(gpt2b, orc, cuda, wmode, kvmode, path):
     assert min(cos) >= 0.999, (min(cos), int(np.argmin(cos)))
 
 
+@pytest.mark.slow
+@pytest.mark.parametrize("wmode,kvmode", [("int8", "floatx"), ("bf16", "floatx"), ("fp8", "8bit")])
+def test_wide_model_persistent_matches_kernel_path(gpt2b, orc, cuda, wmode, kvmode):
+    """C = 1280 (wider than a 4-KB BF16 row), 20 heads, 7 splits of up to 160
+    positions: the persistent kernel against the per-kernel path over 600
+    positions and against the oracle over the first 48."""
+    from cuda_gpt2_inference_b200 import weights
+    cfg = weights.mini_config(L=2, NH=20, maxT=1024, V=500, Vp=512)
+    imgs = _images(gpt2b, cfg, 5, "test")
+    img, sc = imgs[wmode]
+    prompt = [1, 2, 3, 4]
+    ek = _engine(img, wmode, kvmode, sc, "kernels")
+    toks, lk = ek.generate(prompt, 600, want_logits=True)
+    ek.close()
+    seq = list(prompt) + list(toks[:-1])
+    ep = _engine(img, wmode, kvmode, sc, "persistent")
+    _, lp = ep.generate(seq, 0, want_logits=True)
+    ep.close()
+    cos = [cosine(lk[i], lp[i]) for i in range(len(seq))]
+    assert min(cos) >= 0.999, (min(cos), int(np.argmin(cos)))
+    m = orc.Model(img, wmode, kvmode, sc)
+    cos_o = [cosine(lp[i], m.step(int(t), i)) for i, t in enumerate(seq[:48])]
+    assert min(cos_o) >= 0.999, min(cos_o)
+
+
 def test_engine_rejects_bad_inputs(mini, gpt2b):
     cfg, imgs = mini
     eng = _engine(imgs["bf16"][0], "bf16")

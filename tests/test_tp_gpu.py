@@ -1,4 +1,6 @@
-"""Tensor-parallel decode on 2 and 4 GPUs (one process per GPU, NCCL).
+"""Tensor-parallel decode on 2 and 4 GPUs (one process per GPU): the
+persistent kernel with peer stores between the ranks ("p2p") and the
+per-kernel path with NCCL collectives ("nccl").
 
 A GPT-2-XL-shaped miniature (5 heads, uneven over the ranks) in BF16 and
 INT8 + 8-bit KV: the TP group's logits, teacher-forced on the single-GPU
@@ -36,16 +38,24 @@ def _quantize(gpt2b, img16: bytes, fmt: str):
     return out.raw, sc
 
 
-def _rank(rank, size, img, wmode, kvmode, sc, gid, seq, prompt, n_gen, q):
+def _rank(rank, size, port, img, wmode, kvmode, sc, gid, seq, prompt, n_gen, p2p, q):
+    import os
+
     import torch
+    import torch.distributed as dist
     torch.cuda.set_device(rank)
     torch.cuda.synchronize()
-    from cuda_gpt2_inference_b200 import tp
+    from cuda_gpt2_inference_b200 import OPT_PERSISTENT, tp
     try:
-        eng = tp.engine(img, wmode, kvmode, sc, rank, size, gid)
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=size)  # host-side handle exchange only
+        eng = tp.engine(img, wmode, kvmode, sc, rank, size, gid, p2p=p2p)
+        eng.set_option(OPT_PERSISTENT, 1 if p2p else 0)  # fails unless the group is connected
         _, lg = eng.generate(seq, 0, want_logits=True)  # teacher-forced over seq (gathered logits)
         toks, _ = eng.generate(prompt, n_gen)           # device-resident greedy
         eng.close()
+        dist.barrier()
+        dist.destroy_process_group()
         q.put((rank, toks, lg if rank == 0 else None, None))
     except Exception as ex:  # reported to the parent
         q.put((rank, None, None, repr(ex)))
@@ -59,9 +69,17 @@ def mini_xl(gpt2b, cuda):
     return cfg, {"bf16": (img16, None), "int8": _quantize(gpt2b, img16, "int8")}
 
 
+def _free_port() -> int:
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("path", ["p2p", "nccl"])
 @pytest.mark.parametrize("size", [2, 4])
 @pytest.mark.parametrize("wmode,kvmode", [("bf16", "floatx"), ("int8", "8bit")])
-def test_tp_group_matches_single_gpu(mini_xl, orc, gpt2b, wmode, kvmode, size):
+def test_tp_group_matches_single_gpu(mini_xl, orc, gpt2b, wmode, kvmode, size, path):
     if _n_gpus() < size:
         pytest.skip(f"needs {size} GPUs")
     import torch.multiprocessing as mp
@@ -80,7 +98,9 @@ def test_tp_group_matches_single_gpu(mini_xl, orc, gpt2b, wmode, kvmode, size):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     gid = tp.new_group_id()
-    procs = [ctx.Process(target=_rank, args=(r, size, img, wmode, kvmode, sc, gid, seq, prompt, n_gen, q))
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, size, port, img, wmode, kvmode, sc, gid, seq, prompt, n_gen,
+                                             path == "p2p", q))
              for r in range(size)]
     for p in procs:
         p.start()
