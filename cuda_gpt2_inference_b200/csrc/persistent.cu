@@ -123,36 +123,47 @@ __device__ __forceinline__ unsigned long long ll_load_sys(const unsigned long lo
     asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
     return w;
 }
-__device__ __forceinline__ bool aborted(const PersistParams& P) {
-    return *(volatile const int*)P.abort_flag != 0;
-}
+__device__ __forceinline__ bool aborted(const int* flag) { return *(volatile const int*)flag != 0; }
+
+// The exchange arenas of a tensor-parallel group, copied out of the kernel
+// parameters (helpers take this, never the parameter block: indexing the
+// parameters at run time would make the compiler copy all of them to local
+// memory).
+struct PeerSet {
+    unsigned char* x[8];
+    int n, rank;
+    size_t off_abort;
+};
 __device__ __forceinline__ void ll_store_sys(unsigned long long* p, float v, uint32_t tag) {
     const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);
     asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
-// A word of a cross-GPU part to every rank of the group (own copy included).
+// A word of a cross-GPU part to every rank of the group (own copy included);
+// own: this rank's arena (single GPU), ps: the group's arenas.
 template <bool TPG>
-__device__ __forceinline__ void ll_store_group(const PersistParams& P, size_t xoff, size_t word, float v,
-                                               uint32_t tag) {
+__device__ __forceinline__ void ll_store_group(unsigned char* own, const PeerSet* ps, size_t xoff, size_t word,
+                                               float v, uint32_t tag) {
     if constexpr (!TPG) {
-        ll_store(reinterpret_cast<unsigned long long*>(P.peer_x[0] + xoff) + word, v, tag);
+        ll_store(reinterpret_cast<unsigned long long*>(own + xoff) + word, v, tag);
     } else {
-        for (int r = 0; r < P.tp_size; r++)
-            ll_store_sys(reinterpret_cast<unsigned long long*>(P.peer_x[r] + xoff) + word, v, tag);
+        for (int r = 0; r < ps->n; r++)
+            ll_store_sys(reinterpret_cast<unsigned long long*>(ps->x[r] + xoff) + word, v, tag);
     }
 }
-__device__ __noinline__ void give_up(const PersistParams& P) {
+__device__ __noinline__ void give_up(int* flag, const PeerSet* ps) {
     report_device_error(GPT2B_DEVERR_GRID_TIMEOUT);
-    atomicExch(P.abort_flag, 1);
-    for (int r = 0; r < P.tp_size; r++)  // the other ranks leave too
-        if (r != P.tp_rank)
-            asm volatile("st.relaxed.sys.global.b32 [%0], %1;" ::"l"(P.peer_x[r] + P.xoff_abort), "r"(1) : "memory");
+    atomicExch(flag, 1);
+    if (ps)
+        for (int r = 0; r < ps->n; r++)  // the other ranks leave too
+            if (r != ps->rank)
+                asm volatile("st.relaxed.sys.global.b32 [%0], %1;" ::"l"(ps->x[r] + ps->off_abort), "r"(1) : "memory");
 }
 
 // Words i = tid + j*kCT (i < n, j < J) of src into out[j]; all loads of a
 // round are in flight together.  False on timeout (recorded) or abort.
 template <int J, bool SYS>
-__device__ __noinline__ bool ll_gather_j(const PersistParams& P, const unsigned long long* src, int n, uint32_t tag,
+__device__ __noinline__ bool ll_gather_j(int* abort_flag, const PeerSet* ps, const unsigned long long* src, int n,
+                                         uint32_t tag,
                                          float* out) {
     const int tid = threadIdx.x;
     uint32_t pending = 0;
@@ -171,23 +182,23 @@ __device__ __noinline__ bool ll_gather_j(const PersistParams& P, const unsigned 
                 pending &= ~(1u << j);
             }
         if (!pending) break;
-        if (it > kPollLimit) { give_up(P); return false; }
-        if ((it & 15) == 15 && aborted(P)) return false;
+        if (it > kPollLimit) { give_up(abort_flag, ps); return false; }
+        if ((it & 15) == 15 && aborted(abort_flag)) return false;
         __nanosleep(32);
     }
     return true;
 }
 template <bool WIDE>
-__device__ __forceinline__ bool ll_gather(const PersistParams& P, const unsigned long long* src, int n, uint32_t tag,
-                                          float* out) {
-    if constexpr (!WIDE) return ll_gather_j<kGatherJs, false>(P, src, n, tag, out);
-    return n <= kGatherJs * kCT ? ll_gather_j<kGatherJs, false>(P, src, n, tag, out)
-                                : ll_gather_j<kGatherJ, false>(P, src, n, tag, out);
+__device__ __forceinline__ bool ll_gather(int* abort_flag, const PeerSet* ps, const unsigned long long* src, int n,
+                                          uint32_t tag, float* out) {
+    if constexpr (!WIDE) return ll_gather_j<kGatherJs, false>(abort_flag, ps, src, n, tag, out);
+    return n <= kGatherJs * kCT ? ll_gather_j<kGatherJs, false>(abort_flag, ps, src, n, tag, out)
+                                : ll_gather_j<kGatherJ, false>(abort_flag, ps, src, n, tag, out);
 }
 // Words written by the ranks of a tensor-parallel group (system scope, 32-word rounds).
-__device__ __forceinline__ bool ll_gather_group(const PersistParams& P, const unsigned long long* src, int n,
-                                                uint32_t tag, float* out) {
-    return ll_gather_j<kGatherJ, true>(P, src, n, tag, out);
+__device__ __forceinline__ bool ll_gather_group(int* abort_flag, const PeerSet* ps, const unsigned long long* src,
+                                                int n, uint32_t tag, float* out) {
+    return ll_gather_j<kGatherJ, true>(abort_flag, ps, src, n, tag, out);
 }
 
 // consumer-only barriers (named barrier 1, the 256 consumer threads)
@@ -241,19 +252,21 @@ template <> struct PTraits<WK_I8> { using XT = __nv_bfloat16; static constexpr i
 template <> struct PTraits<WK_FP8> { using XT = __nv_bfloat16; static constexpr int kWB = 1; };
 
 // Rows, columns, stage geometry and this CTA's row range of phase `ph` (this
-// rank's shard): K <= C takes 16 rows per stage; wider rows (FCPROJ, K = 4C /
-// tp) 8 rows per stage, in K-parts of at most 2C.
+// rank's shard).  Tensor-core stages (MMA): 16 rows (one tile), rows wider
+// than C in K-parts of C.  CUDA-core stages: 16 rows of K <= C, wider rows 8
+// per stage in K-parts of at most 2C.
 struct PhaseRows {
     int M, K, kparts, part, rs, c0, c1;  // rows, columns, K-parts, columns per part, rows per stage, CTA range
 };
+template <bool MMA>
 __device__ __forceinline__ PhaseRows phase_rows(const PersistParams& P, int ph, int b) {
     PhaseRows r;
     const int C = P.C;
     r.M = (ph == kPhQkv) ? P.qkv_rows : (ph == kPhFc) ? P.fc_rows : (ph == kPhLm) ? P.v_rows : C;
     r.K = (ph == kPhProj) ? P.proj_k : (ph == kPhFcproj) ? P.fcproj_k : C;
-    if (r.K <= C) {
+    if (MMA || r.K <= C) {
         r.rs = kStageUnits;
-        r.kparts = 1;
+        r.kparts = (r.K + C - 1) / C;
     } else {
         r.rs = kStageUnits / 2;
         r.kparts = (r.K + 2 * C - 1) / (2 * C);
@@ -262,6 +275,12 @@ __device__ __forceinline__ PhaseRows phase_rows(const PersistParams& P, int ph, 
     r.c0 = b * r.M / P.G;
     r.c1 = (b + 1) * r.M / P.G;
     return r;
+}
+// Rows of tensor-core stages whose byte length is a multiple of 128 would put
+// the 8 rows of an ldmatrix tile in one bank group: they get 16 bytes of
+// padding.  Other stages keep their rows contiguous (one bulk copy per stage).
+__host__ __device__ __forceinline__ int row_stride(int part_bytes, bool mma) {
+    return (mma && (part_bytes & 127) == 0) ? part_bytes + 16 : part_bytes;
 }
 __device__ __forceinline__ int phase_widx(int ph) { return ph == kPhLm ? 0 : ph + 1; }
 
@@ -344,6 +363,92 @@ __device__ __forceinline__ void chunk_dot2(const uint4& w0, const uint4& w1, con
     }
 }
 
+// ---------------------------------------------------------------------------
+// tensor-core stage products (mma.sync m16n8k16, FP32 accumulation): A = the
+// stage's 16 rows, B = x in column 0 (the other 7 columns zero)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_f16(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// Two codes of a 32-bit word (bytes 0-1 for hi = false, 2-3 for hi = true) as an
+// exact FP16 pair.  INT8: the sign-flipped byte under the FP16 exponent of 1024
+// reads 1024 + code + 128; subtracting 1152 leaves the code.  E4M3: the 7
+// magnitude bits placed as FP16 exponent/mantissa read 2^(e-15) x 1.m (or the
+// FP16 subnormal for e = 0); a multiply by 2^8 rebases the exponent.
+template <int WK>
+__device__ __forceinline__ uint32_t code2_f16x2(uint32_t word, bool hi) {
+    uint32_t r;
+    if constexpr (WK == WK_I8) {
+        const uint32_t h = __byte_perm(word ^ 0x80808080u, 0x64646464u, hi ? 0x4342u : 0x4140u);
+        asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(0x64806480u));
+    } else {
+        const uint32_t w = __byte_perm(word, 0u, hi ? 0x3424u : 0x1404u);  // bytes -> bits 8..15 / 24..31
+        const uint32_t f = (w & 0x80008000u) | ((w & 0x7f007f00u) >> 1);
+        asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(f), "r"(0x5c005c00u));
+    }
+    return r;
+}
+// This warp's share of a stage: 16-column blocks kb = warp, warp + 8, ...
+// (BF16) or 32-column units (8-bit: two MMAs per ldmatrix, the codes of an
+// FP16 pair taken 4 apart, with x loaded in the same order).  Returns, for
+// lanes with (lane & 3) == 0, the partial sums of rows lane/4 (s0) and
+// lane/4 + 8 (s1).
+template <int WK>
+__device__ __forceinline__ void stage_mma(uint32_t a_base, const unsigned char* xb, int part, int warp, int lane,
+                                          float& s0, float& s1) {
+    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const int g = lane >> 2, t = lane & 3;
+    if constexpr (WK == WK_BF16) {
+        const int nkb = part >> 4;
+        for (int kb = warp; kb < nkb; kb += kCW) {
+            uint32_t a0, a1, a2, a3, b0 = 0u, b1 = 0u;
+            ldsm_x4(a_base + (uint32_t)kb * 32u, a0, a1, a2, a3);
+            if (g == 0) {
+                const uint32_t* xw = reinterpret_cast<const uint32_t*>(xb + (size_t)kb * 32);
+                b0 = xw[t];
+                b1 = xw[4 + t];
+            }
+            mma_bf16(d, a0, a1, a2, a3, b0, b1);
+        }
+    } else {
+        const int nku = part >> 5;
+        for (int ku = warp; ku < nku; ku += kCW) {
+            uint32_t r0, r1, r2, r3;
+            ldsm_x4(a_base + (uint32_t)ku * 32u, r0, r1, r2, r3);
+            uint2 x0 = make_uint2(0u, 0u), x1 = make_uint2(0u, 0u);
+            if (g == 0) {
+                const uint2* xw = reinterpret_cast<const uint2*>(xb + (size_t)ku * 64);  // 32 FP16 values
+                x0 = xw[t];
+                x1 = xw[4 + t];
+            }
+            mma_f16(d, code2_f16x2<WK>(r0, false), code2_f16x2<WK>(r1, false), code2_f16x2<WK>(r0, true),
+                    code2_f16x2<WK>(r1, true), x0.x, x0.y);
+            mma_f16(d, code2_f16x2<WK>(r2, false), code2_f16x2<WK>(r3, false), code2_f16x2<WK>(r2, true),
+                    code2_f16x2<WK>(r3, true), x1.x, x1.y);
+        }
+    }
+    s0 = d[0];
+    s1 = d[2];
+}
+
 template <int KV>
 __device__ __forceinline__ float kv_code(uint32_t word, int j) {
     if constexpr (KV == KV_FP8) return e4m3_to_f(word, j);
@@ -365,7 +470,7 @@ __device__ __forceinline__ uint8_t kv_encode(float x, float scale) {
 // shared memory layout
 // ---------------------------------------------------------------------------
 struct PSmem {
-    int stage_bytes, ring, kvbuf, uni, res, lnp, red, misc, bars, total;
+    int stage_bytes, ring, kvbuf, uni, res, lnp, red, xh, mred, misc, bars, total;
 };
 
 template <int WK, int KV>
@@ -376,7 +481,7 @@ __host__ __device__ inline PSmem persist_layout(int C, int ns, int kv_rows, int 
     const bool k8 = (KV == KV_I8 || KV == KV_FP8);
     const int rpp = kCT / (kHSz * kvb / 16);
     PSmem s;
-    s.stage_bytes = kStageUnits * C * wb + kTail;
+    s.stage_bytes = kStageUnits * (C * wb + 16) + kTail;
     int off = 0;
     s.ring = off; off += ns * s.stage_bytes;
     s.kvbuf = off; off += 2 * kv_rows * kHSz * kvb + (k8 ? 2 * (kv_rows + 8) * 4 : 0);
@@ -389,6 +494,8 @@ __host__ __device__ inline PSmem persist_layout(int C, int ns, int kv_rows, int 
     s.res = off; off += C * 4;
     s.lnp = off; off += ((2 * C * xb) + 15) & ~15;  // LayerNorm gamma | beta of the current phase
     s.red = off; off += (tp > 1) ? tp * C * 4 : 0;  // every rank's projection partials
+    s.xh = off; off += (wb == 1) ? 4 * C * 2 : 0;   // x as FP16, the B operand of 8-bit weights
+    s.mred = off; off += 2 * kCW * 16 * 4;           // per-warp row sums of a stage, double-buffered
     s.misc = off; off += kMiscFloats * 4;
     s.bars = off; off += (2 * kMaxNs + 3) * 8;
     s.total = off;
@@ -406,6 +513,8 @@ template <int WK, int KV, int MODE>
 __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const PersistParams P) {
     constexpr bool WIDE = MODE >= 1;
     constexpr bool TPG = MODE == 2;
+    // tensor-core stage products for the wide kernels (8-bit / BF16 weights); CUDA cores otherwise
+    constexpr bool MMA = WIDE && (WK != WK_F32);
     using XT = typename PTraits<WK>::XT;
     constexpr int kWB = PTraits<WK>::kWB;
     constexpr int kXB = (int)sizeof(XT);
@@ -426,6 +535,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
     unsigned char* xs = sm + lay.uni;
     float* res = reinterpret_cast<float*>(sm + lay.res);
     float* red = reinterpret_cast<float*>(sm + lay.red);
+    unsigned char* xh = sm + lay.xh;                      // x as FP16 (8-bit weights)
+    float* mred = reinterpret_cast<float*>(sm + lay.mred);
     float* misc = reinterpret_cast<float*>(sm + lay.misc);
     int* misc_i = reinterpret_cast<int*>(misc);
     volatile int* stop = misc_i + (kMiscFloats - 1);  // consumers left early: the producer stops
@@ -446,6 +557,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int C = P.C, L = P.L, NH = P.NH, maxT = P.maxT, S = P.splits, G = P.G, NS = P.nsw;
+    PeerSet peers;  // tensor parallel only (constant indices into the parameters)
+    const PeerSet* pgp = nullptr;
+    if constexpr (TPG) {
+#pragma unroll
+        for (int r = 0; r < 8; r++) peers.x[r] = P.peer_x[r];
+        peers.n = P.tp_size;
+        peers.rank = P.tp_rank;
+        peers.off_abort = P.xoff_abort;
+        pgp = &peers;
+    }
     const int b = blockIdx.x;
     const int unit_bytes = C * kWB;  // one row-unit: a row of K = C, half a K-half of K = 4C
     const uint32_t epoch0 = *P.d_epoch;
@@ -482,7 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
             for (int u = 0; u <= 4 * L; u++) {
                 const int l = (u == 4 * L) ? 0 : (u >> 2);
                 const int ph = (u == 4 * L) ? kPhLm : (u & 3);
-                const PhaseRows pr = phase_rows(P, ph, b);
+                const PhaseRows pr = phase_rows<MMA>(P, ph, b);
                 const int widx = phase_widx(ph);
                 const int part_bytes = pr.part * kWB;  // per row and stage
                 const size_t row_bytes = (size_t)pr.K * kWB;
@@ -508,7 +629,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                             if (!ok) goto producer_drain;
                         }
                         unsigned char* sd = ring + (size_t)st * lay.stage_bytes;
-                        unsigned char* tail = sd + kStageUnits * unit_bytes;
+                        unsigned char* tail = sd + kStageUnits * (unit_bytes + 16);
                         const bool last = (kq == pr.kparts - 1);
                         uint32_t bb = 0, sb = 0;
                         size_t ba = 0, sa = 0;
@@ -522,11 +643,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                         }
                         PTRACE_STAGE(0, issued);
                         mbar_arrive_expect_tx(&full[st], (uint32_t)(nr * part_bytes) + bb + sb);
-                        if (pr.kparts == 1) {
+                        const int rstride = row_stride(part_bytes, MMA);
+                        if (rstride == part_bytes && pr.kparts == 1) {  // contiguous rows: one copy
                             bulk_g2s(sd, wl + (size_t)r0 * row_bytes, (uint32_t)(nr * part_bytes), &full[st]);
                         } else {
                             for (int i = 0; i < nr; i++)
-                                bulk_g2s(sd + (size_t)i * part_bytes,
+                                bulk_g2s(sd + (size_t)i * rstride,
                                          wl + (size_t)(r0 + i) * row_bytes + (size_t)kq * part_bytes,
                                          (uint32_t)part_bytes, &full[st]);
                         }
@@ -558,6 +680,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
     int kv_issued = 0, kv_uses = 0;
     uint32_t ln_par = 0;    // phase parity of the LayerNorm parameter barrier
     bool ln_pending = false;  // thread 0: a parameter copy is in flight
+    uint32_t consumed_stages = 0;  // selects the mred buffer of a stage
 #ifdef GPT2B_PERSIST_TRACE
     int consumed_n = 0;
 #endif
@@ -579,8 +702,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                 unsigned f;
                 asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(f) : "l"(flag) : "memory");
                 if ((int)(f - need) >= 0) break;
-                if (it > kPollLimit) { give_up(P); bad = true; return; }
-                if ((it & 15) == 15 && aborted(P)) { bad = true; return; }
+                if (it > kPollLimit) { give_up(P.abort_flag, pgp); bad = true; return; }
+                if ((it & 15) == 15 && aborted(P.abort_flag)) { bad = true; return; }
                 __nanosleep(64);
             }
             asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -673,7 +796,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                         const unsigned long long* src = ((ph == kPhFc) ? P.ll_proj : P.ll_fcproj) + lsrc * TP * C;
                         bool ok = true;
                         if constexpr (!TPG) {
-                            ok = ll_gather<WIDE>(P, src, C, tag, gv);
+                            ok = ll_gather<WIDE>(P.abort_flag, pgp, src, C, tag, gv);
 #pragma unroll
                             for (int j = 0; j < kCPT; j++) {
                                 const int c = tid + j * kCT;
@@ -684,7 +807,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                             // order (the same on every rank), rounded as the single-GPU store
                             const int n = TP * C;
                             for (int base = 0; base < n && ok; base += kGatherJ * kCT) {
-                                ok = ll_gather_group(P, src + base, min(n - base, kGatherJ * kCT), tag, gv);
+                                ok = ll_gather_group(P.abort_flag, pgp, src + base, min(n - base, kGatherJ * kCT), tag, gv);
 #pragma unroll
                                 for (int j = 0; j < kGatherJ; j++)
                                     if (base + tid + j * kCT < n) red[base + tid + j * kCT] = gv[j];
@@ -736,17 +859,23 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                         if (c < C) {
                             const float g = WIDE ? to_f<XT>(lnp[c]) : lw[j];
                             const float bb = WIDE ? to_f<XT>(lnp[C + c]) : lb[j];
-                            xv[c] = from_f<XT>((rstd * (res[c] - mean)) * g + bb);
+                            const XT xvv = from_f<XT>((rstd * (res[c] - mean)) * g + bb);
+                            xv[c] = xvv;
+                            if constexpr (w8) reinterpret_cast<__half*>(xh)[c] = __float2half_rn(to_f<XT>(xvv));
                         }
                     }
                 } else {
                     // PROJ: x = atty of this rank's heads; FCPROJ: x = gelu(fc) of this rank's FC rows
                     const int n = (ph == kPhProj) ? P.proj_k : P.fcproj_k;
                     const unsigned long long* src = (ph == kPhProj) ? P.ll_atty + (size_t)l * n : P.ll_fc + (size_t)l * n;
-                    const bool ok = ll_gather<WIDE>(P, src, n, tag, gv);
+                    const bool ok = ll_gather<WIDE>(P.abort_flag, pgp, src, n, tag, gv);
 #pragma unroll
                     for (int j = 0; j < (WIDE ? kGatherJ : kGatherJs); j++)
-                        if (tid + j * kCT < n) xv[tid + j * kCT] = from_f<XT>(gv[j]);
+                        if (tid + j * kCT < n) {
+                            const XT xvv = from_f<XT>(gv[j]);
+                            xv[tid + j * kCT] = xvv;
+                            if constexpr (w8) reinterpret_cast<__half*>(xh)[tid + j * kCT] = __float2half_rn(to_f<XT>(xvv));
+                        }
                     if (cta_any(!ok)) goto consumer_abort;
                 }
                 cta_sync();
@@ -754,7 +883,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
 
                 // ---------- the matrix rows of this CTA ----------
                 {
-                    const PhaseRows pr = phase_rows(P, ph, b);
+                    const PhaseRows pr = phase_rows<MMA>(P, ph, b);
                     unsigned long long* out = nullptr;
                     if (ph == kPhQkv) out = P.ll_qkv + (size_t)l * pr.M;
                     else if (ph == kPhProj) out = P.ll_proj + (size_t)l * pr.M;
@@ -762,12 +891,28 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                     else if (ph == kPhFcproj) out = P.ll_fcproj + (size_t)l * pr.M;
                     const bool has_bias = !lm;
                     const int part_bytes = pr.part * kWB;
-                    const int pc = part_bytes / 16;                   // chunks per row and stage
-                    const bool two = (pr.rs == kStageUnits);         // rows warp and warp + 8
+                    const int rstride = row_stride(part_bytes, MMA);
+                    const int pc = part_bytes / 16;  // chunks per row and stage
+                    // emit one finished row (bias, scale, GELU / partial store / logits)
+                    auto emit = [&](const unsigned char* sd, int r0, int rl, float v) {
+                        const unsigned char* tail = sd + kStageUnits * (unit_bytes + 16);
+                        const int row = r0 + rl;
+                        if constexpr (w8) v *= reinterpret_cast<const float*>(tail + kTailSlot + ((r0 * 4) & 15))[rl];
+                        if (has_bias) v += to_f<XT>(reinterpret_cast<const XT*>(tail + ((r0 * kXB) & 15))[rl]);
+                        if (lm) {
+                            P.logits[row] = v;
+                            if (P.v0 + row < P.V) best_merge(best_v, best_i, v, P.v0 + row);
+                        } else if (ph == kPhProj || ph == kPhFcproj) {  // partials to every rank
+                            ll_store_group<TPG>(P.peer_x[0], pgp, ph == kPhProj ? P.xoff_proj : P.xoff_fcproj,
+                                                ((size_t)l * (TPG ? P.tp_size : 1) + P.tp_rank) * C + row,
+                                                TPG ? v : round_to<XT>(v), tag);
+                        } else {
+                            ll_store(out + row, round_to<XT>(ph == kPhFc ? gelu_tanh(v) : v), tag);
+                        }
+                    };
                     for (int r0 = pr.c0; r0 < pr.c1; r0 += pr.rs) {
                         const int nr = min(pr.rs, pr.c1 - r0);
-                        const bool hA = warp < nr, hB = two && warp + kCW < nr;
-                        float k0 = 0.0f, k1 = 0.0f;
+                        float k0 = 0.0f, k1 = 0.0f;  // running row sums over K-parts
                         for (int kq = 0; kq < pr.kparts; kq++) {
 #ifdef GPT2B_PERSIST_TRACE
                             if (tid == 0) PTRACE_STAGE(1, consumed_n);
@@ -777,60 +922,70 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                             if (tid == 0) PTRACE_STAGE(2, consumed_n);
 #endif
                             const unsigned char* sd = ring + (size_t)cst * lay.stage_bytes;
-                            if (hA) {
-                                const unsigned char* wa = sd + (size_t)warp * part_bytes;
-                                const unsigned char* wb2 = sd + (size_t)(warp + kCW) * part_bytes;
-                                float a0 = 0.0f, a1 = 0.0f;
-                                if (hB) {
-                                    for (int c = lane; c < pc; c += 32)
-                                        chunk_dot2<WK>(*reinterpret_cast<const uint4*>(wa + (size_t)c * 16),
-                                                       *reinterpret_cast<const uint4*>(wb2 + (size_t)c * 16), xs,
-                                                       kq * pc + c, a0, a1);
-                                } else {
-                                    for (int c = lane; c < pc; c += 32)
-                                        a0 += chunk_dot<WK>(*reinterpret_cast<const uint4*>(wa + (size_t)c * 16), xs,
-                                                            kq * pc + c);
-                                }
-#ifdef GPT2B_PERSIST_TRACE
-                                if (tid == 0) PTRACE_STAGE(4, consumed_n);
-#endif
-#pragma unroll
-                                for (int o = 16; o > 0; o >>= 1) {
-                                    a0 += __shfl_xor_sync(0xffffffffu, a0, o);
-                                    a1 += __shfl_xor_sync(0xffffffffu, a1, o);
-                                }
-                                k0 += a0;
-                                k1 += a1;
-#ifdef GPT2B_PERSIST_TRACE
-                                if (tid == 0) PTRACE_STAGE(5, consumed_n);
-#endif
-                                // every lane holds both sums: lane 0 emits row A, lane 1 row B
-                                if (kq == pr.kparts - 1 && (lane == 0 || (lane == 1 && hB))) {
-                                    const unsigned char* tail = sd + kStageUnits * unit_bytes;
-                                    const XT* bw = reinterpret_cast<const XT*>(tail + ((r0 * kXB) & 15));
-                                    const float* sw = reinterpret_cast<const float*>(tail + kTailSlot + ((r0 * 4) & 15));
-                                    const int rl = warp + lane * kCW, row = r0 + rl;
-                                    float v = lane ? k1 : k0;
-                                    if constexpr (w8) v *= sw[rl];
-                                    if (has_bias) v += to_f<XT>(bw[rl]);
-                                    if (lm) {
-                                        P.logits[row] = v;
-                                        if (P.v0 + row < P.V) best_merge(best_v, best_i, v, P.v0 + row);
-                                    } else if (ph == kPhProj || ph == kPhFcproj) {  // partials to every rank
-                                        ll_store_group<TPG>(P, ph == kPhProj ? P.xoff_proj : P.xoff_fcproj,
-                                                            ((size_t)l * (TPG ? P.tp_size : 1) + P.tp_rank) * C + row,
-                                                            TPG ? v : round_to<XT>(v), tag);
+                            const bool last = (kq == pr.kparts - 1);
+                            if constexpr (!MMA) {
+                                // CUDA cores: warp w takes rows w and w + 8
+                                const bool hA = warp < nr, hB = pr.rs == kStageUnits && warp + kCW < nr;
+                                if (hA) {
+                                    const unsigned char* wa = sd + (size_t)warp * rstride;
+                                    const unsigned char* wb2 = sd + (size_t)(warp + kCW) * rstride;
+                                    float a0 = 0.0f, a1 = 0.0f;
+                                    if (hB) {
+                                        for (int c = lane; c < pc; c += 32)
+                                            chunk_dot2<WK>(*reinterpret_cast<const uint4*>(wa + (size_t)c * 16),
+                                                           *reinterpret_cast<const uint4*>(wb2 + (size_t)c * 16), xs,
+                                                           kq * pc + c, a0, a1);
                                     } else {
-                                        ll_store(out + row, round_to<XT>(ph == kPhFc ? gelu_tanh(v) : v), tag);
+                                        for (int c = lane; c < pc; c += 32)
+                                            a0 += chunk_dot<WK>(*reinterpret_cast<const uint4*>(wa + (size_t)c * 16),
+                                                                xs, kq * pc + c);
                                     }
+#pragma unroll
+                                    for (int o = 16; o > 0; o >>= 1) {
+                                        a0 += __shfl_xor_sync(0xffffffffu, a0, o);
+                                        a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+                                    }
+                                    k0 += a0;
+                                    k1 += a1;
+                                    if (last && (lane == 0 || (lane == 1 && hB)))
+                                        emit(sd, r0, warp + lane * kCW, lane ? k1 : k0);
                                 }
+                                __syncwarp();
+                                if (lane == 0) mbar_arrive(&empty[cst]);
+                            } else {
+                                // tensor cores: the 8 warps split K; row sums meet in mred
+                                float s0, s1;
+                                const unsigned char* xb = w8 ? xh + (size_t)kq * pr.part * 2
+                                                             : xs + (size_t)kq * pr.part * 2;
+                                const uint32_t a_base =
+                                    smem_addr(sd) + (uint32_t)((lane & 15) * rstride + (lane >> 4) * 16);
+                                stage_mma<WK>(a_base, xb, pr.part, warp, lane, s0, s1);
+                                __syncwarp();
+                                // warps 1-7 are done with the stage; warp 0 still reads its tail below
+                                if (lane == 0 && warp != 0) mbar_arrive(&empty[cst]);
+                                float* mr = mred + (consumed_stages & 1) * (kCW * 16);
+                                if ((lane & 3) == 0) {
+                                    mr[warp * 16 + (lane >> 2)] = s0;
+                                    mr[warp * 16 + (lane >> 2) + 8] = s1;
+                                }
+                                cta_sync();
+                                if (tid < 16) {  // row tid of the stage: the warps' sums in warp order
+                                    float v = 0.0f;
+#pragma unroll
+                                    for (int w = 0; w < kCW; w++) v += mr[w * 16 + tid];
+                                    k0 += v;
+                                    if (last && tid < nr) emit(sd, r0, tid, k0);
+                                }
+                                if (warp == 0) {
+                                    __syncwarp();
+                                    if (lane == 0) mbar_arrive(&empty[cst]);
+                                }
+                                consumed_stages++;
                             }
-                            __syncwarp();
 #ifdef GPT2B_PERSIST_TRACE
                             if (tid == 0) PTRACE_STAGE(3, consumed_n);
                             consumed_n++;
 #endif
-                            if (lane == 0) mbar_arrive(&empty[cst]);
                             if (++cst == NS) { cst = 0; cpar ^= 1u; }
                         }
                     }
@@ -853,8 +1008,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                         for (uint32_t it = 0;; ++it) {
                             const unsigned long long w = ll_load(src);
                             if ((uint32_t)(w >> 32) == tag) { v = __uint_as_float((uint32_t)w); break; }
-                            if (it > kPollLimit) { give_up(P); bad = true; break; }
-                            if ((it & 15) == 15 && aborted(P)) { bad = true; break; }
+                            if (it > kPollLimit) { give_up(P.abort_flag, pgp); bad = true; break; }
+                            if ((it & 15) == 15 && aborted(P.abort_flag)) { bad = true; break; }
                             __nanosleep(32);
                         }
                         (tid < kHSz ? q_s : (tid < 2 * kHSz ? kcur : vcur))[tid & 63] = v;
@@ -1008,7 +1163,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                     } else {
                         // split 0 merges the head's partials and publishes atty
                         const int nw = (s_eff - 1) * (kHSz + 2);  // <= 31 * 66 <= 8 * kCT
-                        if (!ll_gather<WIDE>(P, part + (kHSz + 2), nw, tag, gv)) bad = true;
+                        if (!ll_gather<WIDE>(P.abort_flag, pgp, part + (kHSz + 2), nw, tag, gv)) bad = true;
 #pragma unroll
                         for (int j = 0; j < 8; j++)
                             if (tid + j * kCT < nw) mrg[tid + j * kCT] = gv[j];
@@ -1045,12 +1200,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                 int bi = misc_i[16];
                 for (int w = 1; w < kCW; w++) best_merge(bv, bi, misc[w], misc_i[16 + w]);
                 const size_t word = 2 * ((size_t)P.tp_rank * G + b);
-                ll_store_group<TPG>(P, P.xoff_lm, word, bv, tag);
-                ll_store_group<TPG>(P, P.xoff_lm, word + 1, __int_as_float(bi), tag);
+                ll_store_group<TPG>(P.peer_x[0], pgp, P.xoff_lm, word, bv, tag);
+                ll_store_group<TPG>(P.peer_x[0], pgp, P.xoff_lm, word + 1, __int_as_float(bi), tag);
             }
             {
-                const bool ok = TPG ? ll_gather_group(P, P.ll_lm, 2 * NG, tag, gv)
-                                    : ll_gather<WIDE>(P, P.ll_lm, 2 * G, tag, gv);
+                const bool ok = TPG ? ll_gather_group(P.abort_flag, pgp, P.ll_lm, 2 * NG, tag, gv)
+                                    : ll_gather<WIDE>(P.abort_flag, pgp, P.ll_lm, 2 * G, tag, gv);
                 float* gvals = reinterpret_cast<float*>(xs);
                 int* gidx = reinterpret_cast<int*>(xs) + NG;
 #pragma unroll
