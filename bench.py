@@ -541,8 +541,12 @@ def run_profile_case(args):
     persistent path)."""
     import cuda_gpt2_inference_b200 as pkg
     from cuda_gpt2_inference_b200.engine import Engine
-    wmode, kvmode = CONFIGS[args.config]
-    cfg, _, img, sc = make_model(wmode, kvmode)
+    if args.config == XL_CONFIG:  # one GPU
+        wmode, kvmode = "int8", "floatx"
+        cfg, img, sc = xl_model(0, 1)
+    else:
+        wmode, kvmode = CONFIGS[args.config]
+        cfg, _, img, sc = make_model(wmode, kvmode)
     eng = Engine.from_buffer(img, wmode, kvmode, sc)
     if args.path == "kernels":
         eng.set_option(pkg.OPT_PERSISTENT, 0)
@@ -570,10 +574,10 @@ def main():
                          "(the 3rd engine launch); prints no bench line")
     args = ap.parse_args()
     rank, local_rank, world = env_rank()
-    if args.config == XL_CONFIG and args.impl == "ours":
-        return run_xl_tp(args, rank, local_rank, world)
     if args.profile_case:
         return run_profile_case(args)
+    if args.config == XL_CONFIG and args.impl == "ours":
+        return run_xl_tp(args, rank, local_rank, world)
     if args.impl == "reference":
         return run_reference(args, rank, world)
     return run_ours(args, rank, local_rank, world)
