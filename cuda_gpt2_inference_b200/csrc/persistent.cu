@@ -257,6 +257,7 @@ template <> struct PTraits<WK_FP8> { using XT = __nv_bfloat16; static constexpr 
 // per stage in K-parts of at most 2C.
 struct PhaseRows {
     int M, K, kparts, part, rs, c0, c1;  // rows, columns, K-parts, columns per part, rows per stage, CTA range
+    int pad;
 };
 template <bool MMA>
 __device__ __forceinline__ PhaseRows phase_rows(const PersistParams& P, int ph, int b) {
@@ -470,7 +471,7 @@ __device__ __forceinline__ uint8_t kv_encode(float x, float scale) {
 // shared memory layout
 // ---------------------------------------------------------------------------
 struct PSmem {
-    int stage_bytes, ring, kvbuf, uni, res, lnp, red, xh, mred, misc, bars, total;
+    int stage_bytes, ring, kvbuf, uni, res, lnp, red, xh, mred, misc, geo, bars, total;
 };
 
 template <int WK, int KV>
@@ -497,6 +498,7 @@ __host__ __device__ inline PSmem persist_layout(int C, int ns, int kv_rows, int 
     s.xh = off; off += (wb == 1) ? 4 * C * 2 : 0;   // x as FP16, the B operand of 8-bit weights
     s.mred = off; off += 2 * kCW * 16 * 4;           // per-warp row sums of a stage, double-buffered
     s.misc = off; off += kMiscFloats * 4;
+    s.geo = off; off += 5 * (int)sizeof(PhaseRows) + 4 * 8;  // this CTA's phase geometry, output bases
     s.bars = off; off += (2 * kMaxNs + 3) * 8;
     s.total = off;
     return s;
@@ -591,6 +593,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
         *stop = 0;
         mbar_fence_init();
     }
+    // the row geometry of every phase and the exchange bases, computed once: the per-phase
+    // paths read them from shared memory (no divisions or parameter loads there)
+    PhaseRows* geo = reinterpret_cast<PhaseRows*>(sm + lay.geo);
+    unsigned long long** obase = reinterpret_cast<unsigned long long**>(sm + lay.geo + 5 * sizeof(PhaseRows));
+    if (tid < 5) {
+        geo[tid] = phase_rows<MMA>(P, tid, b);
+    } else if (tid < 9) {
+        const int k = tid - 5;
+        obase[k] = k == kPhQkv ? P.ll_qkv : (k == kPhProj ? P.ll_proj : (k == kPhFc ? P.ll_fc : P.ll_fcproj));
+    }
     __syncthreads();  // the last block-wide barrier: producer and consumers part here
 
     // =====================================================================
@@ -603,7 +615,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
             for (int u = 0; u <= 4 * L; u++) {
                 const int l = (u == 4 * L) ? 0 : (u >> 2);
                 const int ph = (u == 4 * L) ? kPhLm : (u & 3);
-                const PhaseRows pr = phase_rows<MMA>(P, ph, b);
+                const PhaseRows pr = geo[ph];
                 const int widx = phase_widx(ph);
                 const int part_bytes = pr.part * kWB;  // per row and stage
                 const size_t row_bytes = (size_t)pr.K * kWB;
@@ -883,12 +895,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
 
                 // ---------- the matrix rows of this CTA ----------
                 {
-                    const PhaseRows pr = phase_rows<MMA>(P, ph, b);
-                    unsigned long long* out = nullptr;
-                    if (ph == kPhQkv) out = P.ll_qkv + (size_t)l * pr.M;
-                    else if (ph == kPhProj) out = P.ll_proj + (size_t)l * pr.M;
-                    else if (ph == kPhFc) out = P.ll_fc + (size_t)l * pr.M;
-                    else if (ph == kPhFcproj) out = P.ll_fcproj + (size_t)l * pr.M;
+                    const PhaseRows pr = geo[ph];
+                    unsigned long long* out = lm ? nullptr : obase[ph] + (size_t)l * pr.M;
                     const bool has_bias = !lm;
                     const int part_bytes = pr.part * kWB;
                     const int rstride = row_stride(part_bytes, MMA);
@@ -902,10 +910,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                         if (lm) {
                             P.logits[row] = v;
                             if (P.v0 + row < P.V) best_merge(best_v, best_i, v, P.v0 + row);
-                        } else if (ph == kPhProj || ph == kPhFcproj) {  // partials to every rank
+                        } else if (TPG && (ph == kPhProj || ph == kPhFcproj)) {  // FP32 partials to every rank
                             ll_store_group<TPG>(P.peer_x[0], pgp, ph == kPhProj ? P.xoff_proj : P.xoff_fcproj,
-                                                ((size_t)l * (TPG ? P.tp_size : 1) + P.tp_rank) * C + row,
-                                                TPG ? v : round_to<XT>(v), tag);
+                                                ((size_t)l * P.tp_size + P.tp_rank) * C + row, v, tag);
                         } else {
                             ll_store(out + row, round_to<XT>(ph == kPhFc ? gelu_tanh(v) : v), tag);
                         }
@@ -1046,13 +1053,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                                 dst[d] = from_f<KT>((which ? vcur : kcur)[d]);
                             }
                         }
-                        __threadfence();
-                        cta_sync();
-                        // release this step's tag (a max: the flag never goes back)
-                        if (tid == 0)
-                            asm volatile("red.release.gpu.global.max.u32 [%0], %1;" ::"l"(P.kv_flag + l * NH + ah),
-                                         "r"(tag)
-                                         : "memory");
+                        cta_sync();  // cur8 / cur_sc complete; the flag is released after the partials
                     }
                     float m_run = -FLT_MAX, l_run = 0.0f;
                     float acc[kE];
@@ -1140,11 +1141,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                         }
                     }
                     cta_sync();  // staged rows and p_s consumed
-                    if (tid == 0) {
-                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // after the patch writes
-                        if (l + 1 < L) kv_issue(step, l + 1);
-                        else if (step + 1 < P.n_steps) kv_issue(step + 1, 0);
-                    }
 #pragma unroll
                     for (int e = 0; e < kE; e++) accbuf[rg * kHSz + lp * kE + e] = acc[e];
                     cta_sync();
@@ -1181,7 +1177,20 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                             ll_store(P.ll_atty + (size_t)l * P.proj_k + (size_t)ah * kHSz + tid, round_to<XT>(of / lf), tag);
                         }
                     }
-                    if (cta_any(bad)) goto consumer_abort;  // also carries a failed kv_issue
+                    // off the critical path: the appended K/V row becomes visible before its flag
+                    // (release of this step's tag, a max: the flag never goes back), then the next
+                    // layer's rows are staged (a failed wait there reaches the next cta_any)
+                    if (owns && tid < 2 * kHSz) __threadfence();
+                    if (cta_any(bad)) goto consumer_abort;
+                    if (tid == 0) {
+                        if (owns)
+                            asm volatile("red.release.gpu.global.max.u32 [%0], %1;" ::"l"(P.kv_flag + l * NH + ah),
+                                         "r"(tag)
+                                         : "memory");
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // after the patch writes
+                        if (l + 1 < L) kv_issue(step, l + 1);
+                        else if (step + 1 < P.n_steps) kv_issue(step + 1, 0);
+                    }
                 }
             }
 
