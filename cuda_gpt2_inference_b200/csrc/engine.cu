@@ -416,8 +416,8 @@ cudaError_t setup_persistent(gpt2b_engine* e, int nsm) {
     const int Q = 3 * NHl * 64, A = NHl * 64, F = e->f_l;
     // exchange arena: the cross-GPU parts first, at offsets every rank shares
     // (abort flag, projection and FC-projection partials [L][TP][C], LM pairs
-    // [TP][G][2]), then this rank's own words and flags
-    const size_t n_grp = (size_t)L * TP * C, n_lm = 2 * (size_t)TP * G;
+    // [TP][G] one per kPersistLmStride words), then this rank's own words and flags
+    const size_t n_grp = (size_t)L * TP * C, n_lm = (size_t)kPersistLmStride * TP * G;
     const size_t n_qkv = (size_t)L * Q, n_att = (size_t)L * A, n_fc = (size_t)L * F;
     const size_t n_part = (size_t)L * NHl * S * (64 + 2);
     const size_t off_proj = 256, off_fcproj = off_proj + n_grp * 8, off_lm = off_fcproj + n_grp * 8;

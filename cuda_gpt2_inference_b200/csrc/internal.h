@@ -133,6 +133,9 @@ struct PersistParams {
     float* logits = nullptr;      // Vp floats of the last step
     int n_steps = 0;
 };
+// exchange words between the (value, index) pairs of the LM-head pick: one CTA's
+// pair per 128-byte line (a line shared by several writers is slow to poll)
+constexpr int kPersistLmStride = 16;
 bool persist_supported(int C, int NH, int hs, int maxT, int splits, int nsm);
 int persist_max_splits();
 int persist_max_stages();

@@ -195,6 +195,93 @@ __device__ __forceinline__ bool ll_gather(int* abort_flag, const PeerSet* ps, co
     return n <= kGatherJs * kCT ? ll_gather_j<kGatherJs, false>(abort_flag, ps, src, n, tag, out)
                                 : ll_gather_j<kGatherJ, false>(abort_flag, ps, src, n, tag, out);
 }
+// Words 2q and 2q + 1 for q = tid + j*kCT (j < J2) of src into out[2j], out[2j + 1]: one
+// 16-byte poll per pair (half the requests of word polls; src 16-byte aligned).  False on
+// timeout (recorded) or abort.
+template <int J2, bool SYS>
+__device__ __noinline__ bool ll_gather2_j(int* abort_flag, const PeerSet* ps, const unsigned long long* src, int n,
+                                          uint32_t tag, float* out) {
+    const int tid = threadIdx.x;
+    uint32_t pending = 0;
+#pragma unroll
+    for (int j = 0; j < J2; j++)
+        if (2 * (tid + j * kCT) < n) pending |= 1u << j;
+    for (uint32_t it = 0; pending; ++it) {
+        unsigned long long a[J2], c[J2];
+#pragma unroll
+        for (int j = 0; j < J2; j++) {
+            if (!(pending & (1u << j))) continue;
+            const unsigned long long* p = src + 2 * (tid + j * kCT);
+            if (2 * (tid + j * kCT) + 1 < n) {
+                if (SYS)
+                    asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(a[j]), "=l"(c[j]) : "l"(p) : "memory");
+                else
+                    asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a[j]), "=l"(c[j]) : "l"(p) : "memory");
+            } else {  // an odd count's last word alone
+                a[j] = SYS ? ll_load_sys(p) : ll_load(p);
+                c[j] = (unsigned long long)tag << 32;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < J2; j++)
+            if ((pending & (1u << j)) && (uint32_t)(a[j] >> 32) == tag && (uint32_t)(c[j] >> 32) == tag) {
+                out[2 * j] = __uint_as_float((uint32_t)a[j]);
+                out[2 * j + 1] = __uint_as_float((uint32_t)c[j]);
+                pending &= ~(1u << j);
+            }
+        if (!pending) break;
+        if (it > kPollLimit) { give_up(abort_flag, ps); return false; }
+        if ((it & 15) == 15 && aborted(abort_flag)) return false;
+        __nanosleep(32);
+    }
+    return true;
+}
+template <bool WIDE>
+__device__ __forceinline__ bool ll_gather2(int* abort_flag, const PeerSet* ps, const unsigned long long* src, int n,
+                                           uint32_t tag, float* out) {
+    if constexpr (!WIDE) return ll_gather2_j<kGatherJs / 2, false>(abort_flag, ps, src, n, tag, out);
+    return n <= kGatherJs * kCT ? ll_gather2_j<kGatherJs / 2, false>(abort_flag, ps, src, n, tag, out)
+                                : ll_gather2_j<kGatherJ / 2, false>(abort_flag, ps, src, n, tag, out);
+}
+// Word index of slot j of this thread in a pair gather (and the channel a thread owns in
+// the residual / LayerNorm passes, which follow the same order).
+__device__ __forceinline__ int pair_slot(int tid, int j) { return 2 * (tid + (j >> 1) * kCT) + (j & 1); }
+
+// The LM-head pick: pair k = (value, index bits) at words k * kPersistLmStride + {0, 1},
+// one 16-byte poll per pair, into vals[k] / idx[k] (shared memory).
+template <bool SYS>
+__device__ __noinline__ bool ll_gather_pairs(int* abort_flag, const PeerSet* ps, const unsigned long long* src,
+                                             int npairs, uint32_t tag, float* vals, int* idx) {
+    constexpr int J = kMaxCtas * 8 / kCT + 1;  // pairs per thread (8 ranks of kMaxCtas CTAs)
+    const int tid = threadIdx.x;
+    uint32_t pending = 0;
+#pragma unroll
+    for (int j = 0; j < J; j++)
+        if (tid + j * kCT < npairs) pending |= 1u << j;
+    for (uint32_t it = 0; pending; ++it) {
+#pragma unroll
+        for (int j = 0; j < J; j++) {
+            if (!(pending & (1u << j))) continue;
+            const int k = tid + j * kCT;
+            const unsigned long long* p = src + (size_t)k * kPersistLmStride;
+            unsigned long long a, c;
+            if (SYS)
+                asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(c) : "l"(p) : "memory");
+            else
+                asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(c) : "l"(p) : "memory");
+            if ((uint32_t)(a >> 32) == tag && (uint32_t)(c >> 32) == tag) {
+                vals[k] = __uint_as_float((uint32_t)a);
+                idx[k] = (int)(uint32_t)c;
+                pending &= ~(1u << j);
+            }
+        }
+        if (!pending) break;
+        if (it > kPollLimit) { give_up(abort_flag, ps); return false; }
+        if ((it & 15) == 15 && aborted(abort_flag)) return false;
+        __nanosleep(32);
+    }
+    return true;
+}
 // Words written by the ranks of a tensor-parallel group (system scope, 32-word rounds).
 __device__ __forceinline__ bool ll_gather_group(int* abort_flag, const PeerSet* ps, const unsigned long long* src,
                                                 int n, uint32_t tag, float* out) {
@@ -772,7 +859,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                         const size_t lo = lm ? 0 : (size_t)l * C;
 #pragma unroll
                         for (int j = 0; j < kCPT; j++) {
-                            const int c = tid + j * kCT;
+                            const int c = pair_slot(tid, j);
                             lw[j] = c < C ? to_f<XT>(lnw[lo + c]) : 0.0f;
                             lb[j] = c < C ? to_f<XT>(lnb[lo + c]) : 0.0f;
                         }
@@ -789,7 +876,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                     if (u == 0) {  // embedding: res = round(wte[tok] + wpe[pos]) (encoder_forward_kv)
 #pragma unroll 1
                         for (int j = 0; j < kCPT; j++) {
-                            const int c = tid + j * kCT;
+                            const int c = pair_slot(tid, j);
                             if (c < C) {
                                 float e;
                                 if constexpr (w8) {
@@ -808,10 +895,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                         const unsigned long long* src = ((ph == kPhFc) ? P.ll_proj : P.ll_fcproj) + lsrc * TP * C;
                         bool ok = true;
                         if constexpr (!TPG) {
-                            ok = ll_gather<WIDE>(P.abort_flag, pgp, src, C, tag, gv);
+                            ok = ll_gather2<WIDE>(P.abort_flag, pgp, src, C, tag, gv);
 #pragma unroll
                             for (int j = 0; j < kCPT; j++) {
-                                const int c = tid + j * kCT;
+                                const int c = pair_slot(tid, j);
                                 if (c < C) res[c] = round_to<XT>(res[c] + gv[j]);
                             }
                         } else {
@@ -827,7 +914,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                             cta_sync();
 #pragma unroll
                             for (int j = 0; j < kCPT; j++) {
-                                const int c = tid + j * kCT;
+                                const int c = pair_slot(tid, j);
                                 if (c < C) {
                                     float v = 0.0f;
                                     for (int r = 0; r < TP; r++) v += red[r * C + c];
@@ -841,7 +928,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                     // residual; warp totals in misc[0..7] then misc[8..15], one barrier each
                     float s = 0.0f;
 #pragma unroll
-                    for (int j = 0; j < kCPT; j++) if (tid + j * kCT < C) s += res[tid + j * kCT];
+                    for (int j = 0; j < kCPT; j++) if (pair_slot(tid, j) < C) s += res[pair_slot(tid, j)];
                     s = warp_sum(s);
                     if (lane == 0) misc[warp] = s;
                     cta_sync();
@@ -852,7 +939,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                     float q = 0.0f;
 #pragma unroll
                     for (int j = 0; j < kCPT; j++)
-                        if (tid + j * kCT < C) { const float d = res[tid + j * kCT] - mean; q += d * d; }
+                        if (pair_slot(tid, j) < C) { const float d = res[pair_slot(tid, j)] - mean; q += d * d; }
                     q = warp_sum(q);
                     if (lane == 0) misc[kCW + warp] = q;
                     cta_sync();
@@ -867,7 +954,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                     }
 #pragma unroll
                     for (int j = 0; j < kCPT; j++) {
-                        const int c = tid + j * kCT;
+                        const int c = pair_slot(tid, j);
                         if (c < C) {
                             const float g = WIDE ? to_f<XT>(lnp[c]) : lw[j];
                             const float bb = WIDE ? to_f<XT>(lnp[C + c]) : lb[j];
@@ -880,14 +967,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                     // PROJ: x = atty of this rank's heads; FCPROJ: x = gelu(fc) of this rank's FC rows
                     const int n = (ph == kPhProj) ? P.proj_k : P.fcproj_k;
                     const unsigned long long* src = (ph == kPhProj) ? P.ll_atty + (size_t)l * n : P.ll_fc + (size_t)l * n;
-                    const bool ok = ll_gather<WIDE>(P.abort_flag, pgp, src, n, tag, gv);
+                    const bool ok = ll_gather2<WIDE>(P.abort_flag, pgp, src, n, tag, gv);
 #pragma unroll
-                    for (int j = 0; j < (WIDE ? kGatherJ : kGatherJs); j++)
-                        if (tid + j * kCT < n) {
+                    for (int j = 0; j < (WIDE ? kGatherJ : kGatherJs); j++) {
+                        const int w = pair_slot(tid, j);
+                        if (w < n) {
                             const XT xvv = from_f<XT>(gv[j]);
-                            xv[tid + j * kCT] = xvv;
-                            if constexpr (w8) reinterpret_cast<__half*>(xh)[tid + j * kCT] = __float2half_rn(to_f<XT>(xvv));
+                            xv[w] = xvv;
+                            if constexpr (w8) reinterpret_cast<__half*>(xh)[w] = __float2half_rn(to_f<XT>(xvv));
                         }
+                    }
                     if (cta_any(!ok)) goto consumer_abort;
                 }
                 cta_sync();
@@ -1159,10 +1248,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                     } else {
                         // split 0 merges the head's partials and publishes atty
                         const int nw = (s_eff - 1) * (kHSz + 2);  // <= 31 * 66 <= 8 * kCT
-                        if (!ll_gather<WIDE>(P.abort_flag, pgp, part + (kHSz + 2), nw, tag, gv)) bad = true;
+                        if (!ll_gather2<WIDE>(P.abort_flag, pgp, part + (kHSz + 2), nw, tag, gv)) bad = true;
 #pragma unroll
                         for (int j = 0; j < 8; j++)
-                            if (tid + j * kCT < nw) mrg[tid + j * kCT] = gv[j];
+                            if (pair_slot(tid, j) < nw) mrg[pair_slot(tid, j)] = gv[j];
                         if (cta_any(bad)) goto consumer_abort;
                         if (tid < kHSz) {
                             float mg = m_run;
@@ -1208,23 +1297,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                 float bv = misc[0];
                 int bi = misc_i[16];
                 for (int w = 1; w < kCW; w++) best_merge(bv, bi, misc[w], misc_i[16 + w]);
-                const size_t word = 2 * ((size_t)P.tp_rank * G + b);
+                const size_t word = (size_t)kPersistLmStride * ((size_t)P.tp_rank * G + b);
                 ll_store_group<TPG>(P.peer_x[0], pgp, P.xoff_lm, word, bv, tag);
                 ll_store_group<TPG>(P.peer_x[0], pgp, P.xoff_lm, word + 1, __int_as_float(bi), tag);
             }
             {
-                const bool ok = TPG ? ll_gather_group(P.abort_flag, pgp, P.ll_lm, 2 * NG, tag, gv)
-                                    : ll_gather<WIDE>(P.abort_flag, pgp, P.ll_lm, 2 * G, tag, gv);
                 float* gvals = reinterpret_cast<float*>(xs);
                 int* gidx = reinterpret_cast<int*>(xs) + NG;
-#pragma unroll
-                for (int j = 0; j < (TPG ? kGatherJ : 2); j++) {
-                    const int wi = tid + j * kCT;
-                    if (wi < 2 * NG) {
-                        if (wi & 1) gidx[wi >> 1] = __float_as_int(gv[j]);
-                        else gvals[wi >> 1] = gv[j];
-                    }
-                }
+                const bool ok = ll_gather_pairs<TPG>(P.abort_flag, pgp, P.ll_lm, NG, tag, gvals, gidx);
                 if (cta_any(!ok)) goto consumer_abort;
                 PTRACE(4 * L * 3 + 2);
                 float bv = -FLT_MAX;
