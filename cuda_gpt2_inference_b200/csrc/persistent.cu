@@ -1006,6 +1006,60 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                             ll_store(out + row, round_to<XT>(ph == kPhFc ? gelu_tanh(v) : v), tag);
                         }
                     };
+                    if (!MMA && lm) {
+                        // the LM head on CUDA cores, two stages per round: warp w takes rows w and
+                        // w + 8 of both (four sums sharing every x load); one K-part per row
+                        for (int r0 = pr.c0; r0 < pr.c1; r0 += 2 * pr.rs) {
+                            const int na = min(pr.rs, pr.c1 - r0), nb = min(pr.rs, pr.c1 - r0 - pr.rs);
+                            const int cb = cst + 1 == NS ? 0 : cst + 1;
+                            const uint32_t pb = cst + 1 == NS ? cpar ^ 1u : cpar;
+                            if (!mbar_wait(&full[cst], cpar)) bad = true;
+                            if (nb > 0 && !mbar_wait(&full[cb], pb)) bad = true;
+                            const unsigned char* sa = ring + (size_t)cst * lay.stage_bytes;
+                            const unsigned char* sb = ring + (size_t)cb * lay.stage_bytes;
+                            const bool a1v = warp + kCW < na, b0v = warp < nb, b1v = warp + kCW < nb;
+                            if (warp < na) {
+                                const unsigned char* w0 = sa + (size_t)warp * part_bytes;
+                                const unsigned char* w1 = sa + (size_t)(a1v ? warp + kCW : warp) * part_bytes;
+                                const unsigned char* w2 = sb + (size_t)(b0v ? warp : 0) * part_bytes;
+                                const unsigned char* w3 = sb + (size_t)(b1v ? warp + kCW : 0) * part_bytes;
+                                float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+                                if (nb > 0) {
+                                    for (int c = lane; c < pc; c += 32) {
+                                        chunk_dot2<WK>(*reinterpret_cast<const uint4*>(w0 + (size_t)c * 16),
+                                                       *reinterpret_cast<const uint4*>(w1 + (size_t)c * 16), xs, c, a0, a1);
+                                        chunk_dot2<WK>(*reinterpret_cast<const uint4*>(w2 + (size_t)c * 16),
+                                                       *reinterpret_cast<const uint4*>(w3 + (size_t)c * 16), xs, c, a2, a3);
+                                    }
+                                } else {
+                                    for (int c = lane; c < pc; c += 32)
+                                        chunk_dot2<WK>(*reinterpret_cast<const uint4*>(w0 + (size_t)c * 16),
+                                                       *reinterpret_cast<const uint4*>(w1 + (size_t)c * 16), xs, c, a0, a1);
+                                }
+#pragma unroll
+                                for (int o = 16; o > 0; o >>= 1) {
+                                    a0 += __shfl_xor_sync(0xffffffffu, a0, o);
+                                    a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+                                    a2 += __shfl_xor_sync(0xffffffffu, a2, o);
+                                    a3 += __shfl_xor_sync(0xffffffffu, a3, o);
+                                }
+                                if (lane == 0) emit(sa, r0, warp, a0);
+                                if (lane == 1 && a1v) emit(sa, r0, warp + kCW, a1);
+                                if (lane == 2 && b0v) emit(sb, r0 + pr.rs, warp, a2);
+                                if (lane == 3 && b1v) emit(sb, r0 + pr.rs, warp + kCW, a3);
+                            }
+                            __syncwarp();
+                            if (lane == 0) {
+                                mbar_arrive(&empty[cst]);
+                                if (nb > 0) mbar_arrive(&empty[cb]);
+                            }
+                            if (++cst == NS) { cst = 0; cpar ^= 1u; }
+                            if (nb > 0 && ++cst == NS) { cst = 0; cpar ^= 1u; }
+#ifdef GPT2B_PERSIST_TRACE
+                            consumed_n += nb > 0 ? 2 : 1;
+#endif
+                        }
+                    } else
                     for (int r0 = pr.c0; r0 < pr.c1; r0 += pr.rs) {
                         const int nr = min(pr.rs, pr.c1 - r0);
                         float k0 = 0.0f, k1 = 0.0f;  // running row sums over K-parts
