@@ -302,26 +302,6 @@ __device__ __forceinline__ bool cta_any(bool v) {
         : "memory");
     return r != 0;
 }
-__device__ __forceinline__ float cta_sum(float v, float* scratch) {
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    v = warp_sum(v);
-    if (lane == 0) scratch[w] = v;
-    cta_sync();
-    float t = (lane < kCW) ? scratch[lane] : 0.0f;
-    t = warp_sum(t);
-    cta_sync();
-    return t;
-}
-__device__ __forceinline__ float cta_max(float v, float* scratch) {
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    v = warp_max(v);
-    if (lane == 0) scratch[w] = v;
-    cta_sync();
-    float t = (lane < kCW) ? scratch[lane] : -FLT_MAX;
-    t = warp_max(t);
-    cta_sync();
-    return t;
-}
 __device__ __forceinline__ void best_merge(float& bv, int& bi, float ov, int oi) {
     if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
 }
@@ -1225,8 +1205,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                         if (cta_any(bad)) goto consumer_abort;
                         const unsigned char* Kst = kvbuf;
                         const unsigned char* Vst = kvbuf + kKvRows * kRowB;
-                        // scores (the per-kernel engine attention's arithmetic)
-                        for (int rbase = 0; rbase < n_local; rbase += kRPP) {
+                        // warp-local softmax: warp w's row groups take rows rbase + rg of every pass;
+                        // each warp keeps its own (max, exp-sum, un-normalised out) and the warps'
+                        // states merge behind one barrier (the online-softmax combine)
+                        float mw = -FLT_MAX;
+                        for (int rbase = 0; rbase < n_local; rbase += kRPP) {  // scores
                             const int r = rbase + rg;
                             const bool valid = r < n_local;
                             const uint4 w = valid ? *reinterpret_cast<const uint4*>(Kst + r * kRowB + lp * 16)
@@ -1249,20 +1232,20 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                             }
 #pragma unroll
                             for (int o = kLP / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-                            if (lp == 0 && valid) {
+                            if (valid) {
                                 if constexpr (k8) d *= ksc[r];
-                                p_s[r] = d * P.attn_scale;
+                                d *= P.attn_scale;
+                                mw = fmaxf(mw, d);
+                                if (lp == 0) p_s[r] = d;
                             }
                         }
-                        cta_sync();
-                        // one chunk: the online-softmax state starts at (-FLT_MAX, 0)
-                        m_run = cta_max(tid < n_local ? p_s[tid] : -FLT_MAX, misc);
-                        float ev = 0.0f;
-                        if (tid < n_local) { ev = __expf(p_s[tid] - m_run); p_s[tid] = ev; }
-                        l_run = cta_sum(ev, misc);  // ends with a barrier: p_s is complete
-                        for (int r = rg; r < n_local; r += kRPP) {
+                        mw = warp_max(mw);
+                        __syncwarp();  // this warp's scores in p_s
+                        float lw = 0.0f;
+                        for (int r = rg; r < n_local; r += kRPP) {  // exp and P.V of the same rows
+                            const float p = __expf(p_s[r] - mw);
+                            if (lp == 0) lw += p;
                             const uint4 w = *reinterpret_cast<const uint4*>(Vst + r * kRowB + lp * 16);
-                            const float p = p_s[r];
                             if constexpr (KV == KV_F32) {
                                 acc[0] += p * __uint_as_float(w.x); acc[1] += p * __uint_as_float(w.y);
                                 acc[2] += p * __uint_as_float(w.z); acc[3] += p * __uint_as_float(w.w);
@@ -1282,14 +1265,33 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                                     for (int j = 0; j < 4; j++) acc[4 * i + j] += pv * kv_code<KV>(ww[i], j);
                             }
                         }
-                    }
-                    cta_sync();  // staged rows and p_s consumed
+                        lw = warp_sum(lw);
 #pragma unroll
-                    for (int e = 0; e < kE; e++) accbuf[rg * kHSz + lp * kE + e] = acc[e];
-                    cta_sync();
+                        for (int o = kLP; o < 32; o <<= 1)  // the warp's row groups: lanes with equal lp
+#pragma unroll
+                            for (int e = 0; e < kE; e++) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
+                        float* ws = accbuf + warp * (kHSz + 2);
+                        if (lane < kLP) {
+#pragma unroll
+                            for (int e = 0; e < kE; e++) ws[lp * kE + e] = acc[e];
+                        }
+                        if (lane == 0) { ws[kHSz] = mw; ws[kHSz + 1] = lw; }
+                    }
+                    cta_sync();  // staged rows consumed; every warp's state in accbuf
                     float o = 0.0f;
-                    if (tid < kHSz)
-                        for (int g = 0; g < kRPP; g++) o += accbuf[g * kHSz + tid];
+                    if (n_local > 0) {
+                        float sw[kCW];
+#pragma unroll
+                        for (int w = 0; w < kCW; w++) m_run = fmaxf(m_run, accbuf[w * (kHSz + 2) + kHSz]);
+#pragma unroll
+                        for (int w = 0; w < kCW; w++) {
+                            sw[w] = __expf(accbuf[w * (kHSz + 2) + kHSz] - m_run);
+                            l_run += sw[w] * accbuf[w * (kHSz + 2) + kHSz + 1];
+                        }
+                        if (tid < kHSz)
+#pragma unroll
+                            for (int w = 0; w < kCW; w++) o += sw[w] * accbuf[w * (kHSz + 2) + tid];
+                    }
                     PTRACE(u * 3 + 2);
                     unsigned long long* part = P.ll_part + ((size_t)l * NH + ah) * S * (kHSz + 2);
                     if (as > 0) {
@@ -1308,10 +1310,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                             if (pair_slot(tid, j) < nw) mrg[pair_slot(tid, j)] = gv[j];
                         if (cta_any(bad)) goto consumer_abort;
                         if (tid < kHSz) {
+                            // unrolled: the loads and exponentials of several splits in flight together
                             float mg = m_run;
+#pragma unroll 4
                             for (int k = 0; k < s_eff - 1; k++) mg = fmaxf(mg, mrg[k * (kHSz + 2) + kHSz]);
                             const float r0 = __expf(m_run - mg);
                             float of = 0.0f + r0 * o, lf = 0.0f + r0 * l_run;
+#pragma unroll 4
                             for (int k = 0; k < s_eff - 1; k++) {
                                 const float rs = __expf(mrg[k * (kHSz + 2) + kHSz] - mg);
                                 of += rs * mrg[k * (kHSz + 2) + tid];
