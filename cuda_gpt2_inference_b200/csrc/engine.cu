@@ -393,8 +393,8 @@ __global__ void set_history_kernel(int* history, const int* d_token, const int* 
 }
 
 // Plans the persistent decode kernel when the shape allows it: splits per
-// head (as many as fill the SMs, at most 96 positions each), ring stages per
-// warp (as many as fit in shared memory), and the zero-initialised exchange
+// head (as many as fill the SMs, at most 96 positions each), ring stages (as
+// many as fit in shared memory, at most kPersistRingBytes of weights), and the zero-initialised exchange
 // arena: tagged words per layer and phase, per-(layer, head) KV flags, the
 // epoch counter and the abort flag.
 cudaError_t setup_persistent(gpt2b_engine* e, int nsm) {
@@ -407,7 +407,8 @@ cudaError_t setup_persistent(gpt2b_engine* e, int nsm) {
     if (!coop || TP > 8 || !persist_supported(C, NHl, 64, maxT, S, nsm)) return cudaSuccess;
     const int kv_rows = engine_attn_chunk(maxT, S);
     int nsw = 0;
-    for (int k = persist_max_stages(); k >= 2 && !nsw; k--) {
+    const int kcap = std::max(2, std::min(persist_max_stages(), kPersistRingBytes / persist_stage_bytes(e->wk, C)));
+    for (int k = kcap; k >= 2 && !nsw; k--) {
         const int b = persist_smem_bytes(e->wk, e->kvk, C, k, kv_rows, TP);
         if (b > 0 && b <= max_dyn_smem()) nsw = k;
     }

@@ -139,6 +139,11 @@ constexpr int kPersistLmStride = 16;
 bool persist_supported(int C, int NH, int hs, int maxT, int splits, int nsm);
 int persist_max_splits();
 int persist_max_stages();
+int persist_stage_bytes(int wk, int C);  // one ring stage: 16 row-units of C weights + bias/scale tail
+// Weight bytes the ring holds at most: deeper look-ahead measured slower on B200 (GPT-2 124M:
+// 4 BF16 / 8 INT8 stages beat the 7 / 14 that fit; the extra copies only add HBM traffic
+// while the CTAs wait on exchange words).
+constexpr int kPersistRingBytes = 104 * 1024;
 int persist_smem_bytes(int wk, int kv, int C, int nsw, int kv_rows, int tp);  // -1: unsupported, or no fit
 cudaError_t launch_persistent(int wk, int kv, const PersistParams& P, cudaStream_t st);
 

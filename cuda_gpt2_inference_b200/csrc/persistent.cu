@@ -1485,6 +1485,8 @@ bool persist_supported(int C, int NH, int hs, int maxT, int splits, int nsm) {
 int persist_max_splits() { return kMaxSplits; }
 int persist_max_stages() { return kMaxNs; }
 
+int persist_stage_bytes(int wk, int C) { return kStageUnits * (C * wkind_bytes(wk) + 16) + kTail; }
+
 cudaError_t launch_persistent(int wk, int kv, const PersistParams& P, cudaStream_t st) {
     return persist_dispatch(wk, kv, P, st, nullptr);
 }
