@@ -904,29 +904,27 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                         }
                         if (cta_any(!ok)) goto consumer_abort;
                     }
-                    // LayerNorm (layernorm.cuh:171-241): two passes over the rounded
-                    // residual; warp totals in misc[0..7] then misc[8..15], one barrier each
-                    float s = 0.0f;
-#pragma unroll
-                    for (int j = 0; j < kCPT; j++) if (pair_slot(tid, j) < C) s += res[pair_slot(tid, j)];
-                    s = warp_sum(s);
-                    if (lane == 0) misc[warp] = s;
-                    cta_sync();
-                    s = 0.0f;
-#pragma unroll
-                    for (int w = 0; w < kCW; w++) s += misc[w];
-                    const float mean = s / (float)C;
-                    float q = 0.0f;
+                    // LayerNorm (layernorm.cuh:171-241) statistics in one pass: sum and sum of
+                    // squares of the rounded residual, warp totals in misc[0..15], one barrier
+                    // (var = E[x^2] - mean^2 in FP32; the two-pass form costs a second barrier
+                    // and measured 2 % slower per token)
+                    float s = 0.0f, q = 0.0f;
 #pragma unroll
                     for (int j = 0; j < kCPT; j++)
-                        if (pair_slot(tid, j) < C) { const float d = res[pair_slot(tid, j)] - mean; q += d * d; }
-                    q = warp_sum(q);
-                    if (lane == 0) misc[kCW + warp] = q;
+                        if (pair_slot(tid, j) < C) { const float v = res[pair_slot(tid, j)]; s += v; q += v * v; }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) {
+                        s += __shfl_xor_sync(0xffffffffu, s, o);
+                        q += __shfl_xor_sync(0xffffffffu, q, o);
+                    }
+                    if (lane == 0) { misc[warp] = s; misc[kCW + warp] = q; }
                     cta_sync();
+                    s = 0.0f;
                     q = 0.0f;
 #pragma unroll
-                    for (int w = 0; w < kCW; w++) q += misc[kCW + w];
-                    const float rstd = rsqrtf(q / (float)C + 1e-5f);
+                    for (int w = 0; w < kCW; w++) { s += misc[w]; q += misc[kCW + w]; }
+                    const float mean = s / (float)C;
+                    const float rstd = rsqrtf(fmaxf(q / (float)C - mean * mean, 0.0f) + 1e-5f);
                     if constexpr (WIDE) {
                         if (!mbar_wait(ln_bar, ln_par)) bad = true;
                         ln_par ^= 1u;
@@ -1037,6 +1035,43 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                             if (nb > 0 && ++cst == NS) { cst = 0; cpar ^= 1u; }
 #ifdef GPT2B_PERSIST_TRACE
                             consumed_n += nb > 0 ? 2 : 1;
+#endif
+                        }
+                    } else if (!MMA && pr.kparts == 2) {
+                        // CUDA cores, rows wider than C: both K-parts of a row block in one round
+                        // (warp w: row w, one sum per part, added in part order)
+                        for (int r0 = pr.c0; r0 < pr.c1; r0 += pr.rs) {
+                            const int nr = min(pr.rs, pr.c1 - r0);
+                            const int cb = cst + 1 == NS ? 0 : cst + 1;
+                            const uint32_t pb = cst + 1 == NS ? cpar ^ 1u : cpar;
+                            if (!mbar_wait(&full[cst], cpar)) bad = true;
+                            if (!mbar_wait(&full[cb], pb)) bad = true;
+                            const unsigned char* sa = ring + (size_t)cst * lay.stage_bytes;
+                            const unsigned char* sb = ring + (size_t)cb * lay.stage_bytes;
+                            if (warp < nr) {
+                                const unsigned char* wa = sa + (size_t)warp * rstride;
+                                const unsigned char* wb2 = sb + (size_t)warp * rstride;
+                                float a0 = 0.0f, a1 = 0.0f;
+                                for (int c = lane; c < pc; c += 32) {
+                                    a0 += chunk_dot<WK>(*reinterpret_cast<const uint4*>(wa + (size_t)c * 16), xs, c);
+                                    a1 += chunk_dot<WK>(*reinterpret_cast<const uint4*>(wb2 + (size_t)c * 16), xs, pc + c);
+                                }
+#pragma unroll
+                                for (int o = 16; o > 0; o >>= 1) {
+                                    a0 += __shfl_xor_sync(0xffffffffu, a0, o);
+                                    a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+                                }
+                                if (lane == 0) emit(sb, r0, warp, (0.0f + a0) + a1);
+                            }
+                            __syncwarp();
+                            if (lane == 0) {
+                                mbar_arrive(&empty[cst]);
+                                mbar_arrive(&empty[cb]);
+                            }
+                            for (int k = 0; k < 2; k++)
+                                if (++cst == NS) { cst = 0; cpar ^= 1u; }
+#ifdef GPT2B_PERSIST_TRACE
+                            consumed_n += 2;
 #endif
                         }
                     } else
