@@ -188,13 +188,6 @@ __device__ __noinline__ bool ll_gather_j(int* abort_flag, const PeerSet* ps, con
     }
     return true;
 }
-template <bool WIDE>
-__device__ __forceinline__ bool ll_gather(int* abort_flag, const PeerSet* ps, const unsigned long long* src, int n,
-                                          uint32_t tag, float* out) {
-    if constexpr (!WIDE) return ll_gather_j<kGatherJs, false>(abort_flag, ps, src, n, tag, out);
-    return n <= kGatherJs * kCT ? ll_gather_j<kGatherJs, false>(abort_flag, ps, src, n, tag, out)
-                                : ll_gather_j<kGatherJ, false>(abort_flag, ps, src, n, tag, out);
-}
 // Words 2q and 2q + 1 for q = tid + j*kCT (j < J2) of src into out[2j], out[2j + 1]: one
 // 16-byte poll per pair (half the requests of word polls; src 16-byte aligned).  False on
 // timeout (recorded) or abort.
