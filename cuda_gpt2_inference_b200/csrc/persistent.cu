@@ -807,6 +807,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
     {
         const XT* wpe = reinterpret_cast<const XT*>(P.wpe);
         float gv[(WIDE || TPG) ? kGatherJ : kGatherJs];
+        float ln_shift = 0.0f;  // the last LayerNorm's mean (the same in every consumer thread)
         for (int step = 0; step < P.n_steps; step++) {
             const uint32_t tag = epoch0 + (uint32_t)step + 1u;
             const int pos = pos0 + step;
@@ -899,12 +900,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                     }
                     // LayerNorm (layernorm.cuh:171-241) statistics in one pass: sum and sum of
                     // squares of the rounded residual, warp totals in misc[0..15], one barrier
-                    // (var = E[x^2] - mean^2 in FP32; the two-pass form costs a second barrier
-                    // and measured 2 % slower per token)
+                    // (the two-pass form costs a second barrier and measured 2 % slower per
+                    // token).  The sums are taken about the previous LayerNorm's mean, so the
+                    // variance E[(x-k)^2] - E[x-k]^2 does not cancel when a row's mean is large
+                    // against its spread
                     float s = 0.0f, q = 0.0f;
 #pragma unroll
                     for (int j = 0; j < kCPT; j++)
-                        if (pair_slot(tid, j) < C) { const float v = res[pair_slot(tid, j)]; s += v; q += v * v; }
+                        if (pair_slot(tid, j) < C) {
+                            const float v = res[pair_slot(tid, j)] - ln_shift;
+                            s += v;
+                            q += v * v;
+                        }
 #pragma unroll
                     for (int o = 16; o > 0; o >>= 1) {
                         s += __shfl_xor_sync(0xffffffffu, s, o);
@@ -916,8 +923,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                     q = 0.0f;
 #pragma unroll
                     for (int w = 0; w < kCW; w++) { s += misc[w]; q += misc[kCW + w]; }
-                    const float mean = s / (float)C;
-                    const float rstd = rsqrtf(fmaxf(q / (float)C - mean * mean, 0.0f) + 1e-5f);
+                    const float ms = s / (float)C;
+                    const float mean = ln_shift + ms;
+                    const float rstd = rsqrtf(fmaxf(q / (float)C - ms * ms, 0.0f) + 1e-5f);
+                    ln_shift = mean;
                     if constexpr (WIDE) {
                         if (!mbar_wait(ln_bar, ln_par)) bad = true;
                         ln_par ^= 1u;
