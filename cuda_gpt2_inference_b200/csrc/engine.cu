@@ -123,7 +123,7 @@ void param_sizes(const gpt2b_config& c, size_t n[16]) {
 // tensors stored as 8-bit codes in the mixed file (quantize.cu:190-196)
 const int kLinearSlot[16] = {0, -1, -1, -1, 1, -1, 2, -1, -1, -1, 3, -1, 4, -1, -1, -1};
 
-// Tensor-parallel shard of one rank (SURVEY-style Megatron split for decode):
+// Tensor-parallel shard of one rank (the Megatron column/row split, for decode):
 // QKV and FC column-parallel (heads, FC rows), attention projection and FC
 // projection row-parallel (their K slices), LM head vocab-parallel.  25 heads
 // split unevenly (13/12, 7/6/6/6, 4/3x7); FC rows and vocab rows evenly.

@@ -193,9 +193,11 @@ int gpt2b_attention_kv_merge_f32(float* out, const float* part_out, const float*
  * held until the process exits): B*NH*S must not exceed 2048, else
  * GPT2B_ERR_INVALID_ARG.  Allocates nothing.  The first call on a device looks
  * up that array's device address (cudaGetSymbolAddress), so make that first
- * call before any stream capture.  All calls share the one array: calls that
- * can overlap on the GPU (different streams, or different host threads on the
- * same device) race and must be serialised by the caller. */
+ * call before any stream capture.  That address is kept per device ordinal for
+ * the life of the process; after cudaDeviceReset on a device it is stale, so do
+ * not call this entry point on a device that was reset.  All calls share the
+ * one array: calls that can overlap on the GPU (different streams, or different
+ * host threads on the same device) race and must be serialised by the caller. */
 int gpt2b_attention_forward_kv_large_bf16_noalloc(uint16_t* out, const uint16_t* qkv, const uint16_t* kv_cache, int B,
                                                   int NH, int hs, int maxT, const int* d_pos, int S,
                                                   gpt2b_stream_t stream);

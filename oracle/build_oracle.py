@@ -27,7 +27,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 BUILD = os.path.join(HERE, "_build")
 REF_OUT = os.path.join(HERE, "_ref")
 SHIMS = os.path.join(HERE, "ref_shims")
-DEFAULT_REFERENCE = os.environ.get("GPT2B_REFERENCE_DIR", "/root/reference")
+# The reference checkout: $GPT2B_REFERENCE_DIR, else a directory named "reference"
+# beside this repository's root (absent on hosts that only run prebuilt files).
+DEFAULT_REFERENCE = (os.environ.get("GPT2B_REFERENCE_DIR")
+                     or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -32,8 +32,12 @@ def _engine(img, wmode, kvmode="floatx", sc=None, path="persistent"):
     """An engine on the requested step implementation (fails if it is unavailable)."""
     from cuda_gpt2_inference_b200 import OPT_PERSISTENT
     from cuda_gpt2_inference_b200.engine import Engine
+    assert path in PATHS, path
     eng = Engine.from_buffer(img, wmode, kvmode, sc)
     eng.set_option(OPT_PERSISTENT, 1 if path == "persistent" else 0)
+    # a silent fallback to the other implementation fails here: the persistent
+    # kernel reports 0 kernels per step (one launch per call)
+    assert (eng.kernels_per_step() == 0) == (path == "persistent"), (path, eng.kernels_per_step())
     return eng
 
 
@@ -248,11 +252,11 @@ def _ref_engine(orc, name, path):
 def test_124m_against_reference_engine(m124, orc, tmp_path, wmode, kvmode, refname, path):
     cfg, imgs = m124
     img, sc = imgs[wmode]
-    path = tmp_path / "model.bin"
-    path.write_bytes(img)
+    model_file = tmp_path / "model.bin"
+    model_file.write_bytes(img)
     if sc is not None:
         (tmp_path / "model_scales.bin").write_bytes(sc.tobytes())
-    ref = _ref_engine(orc, refname, path)
+    ref = _ref_engine(orc, refname, model_file)
     rng = np.random.default_rng(5)
     prompt = rng.integers(0, cfg["V"], 24).astype(np.int32)
     n_gen = 176  # crosses the reference's 150-position switch to split+merge

@@ -250,16 +250,25 @@ def test_attention_against_reference_kernels(cuda, orc, pos):
     assert np.allclose(outs["mine"][3], outs["ref"][3], rtol=1e-5, atol=1e-5)  # split maxima
     assert np.allclose(outs["mine"][2], outs["ref"][2], rtol=1e-4, atol=1e-6)  # split exp-sums
     assert np.allclose(outs["mine"][1], outs["ref"][1], rtol=1e-3, atol=1e-4)  # un-normalised partials
-    w8 = _ref_lib(orc, "w8_int8")
-    if w8 is not None:
+    # 8-bit KV append: codes and scales byte-identical with kv_cache_write_kernel_w8
+    # (attention_kvcache_w8.cuh:115-155) built for INT8 and for FP8 E4M3
+    checked = 0
+    for kind in ("int8", "fp8"):
+        w8 = _ref_lib(orc, f"w8_{kind}")
+        if w8 is None:
+            continue
         ca = torch.zeros(2 * NH * maxT * hs, dtype=torch.uint8, device="cuda")
         cb = ca.clone()
         sa, sb = torch.zeros(2 * NH * maxT, device="cuda"), torch.zeros(2 * NH * maxT, device="cuda")
-        ops.kv_cache_write(ca, qd, 1, NH, hs, maxT, dpos, kv_scale=sa, fmt="int8")
-        w8.ref_set_cur_len(pos)
+        ops.kv_cache_write(ca, qd, 1, NH, hs, maxT, dpos, kv_scale=sa, fmt=kind)
+        assert w8.ref_set_cur_len(pos) == 0
         w8.ref_kv_cache_write_w8(vp(cb), vp(sb), vp(qd), 1, NH, hs, maxT)
         torch.cuda.synchronize()
-        assert torch.equal(ca, cb) and torch.equal(sa, sb)
+        assert torch.equal(ca, cb), kind
+        assert torch.equal(sa, sb), kind
+        assert int(torch.count_nonzero(ca)) > 0, kind  # the row at pos was written
+        checked += 1
+    assert checked == 2, "reference 8-bit kernels (INT8 and FP8) not built"
 
 
 # ------------------------------------------------------ LayerNorm etc. ----

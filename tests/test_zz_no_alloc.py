@@ -4,7 +4,7 @@ Some callers cannot give the library scratch memory (their memory pool owns
 the whole device, or cudaMalloc's implicit synchronisation is off-limits on
 their hot path).  gpt2b_attention_forward_kv_large_bf16_noalloc keeps the
 split partials in a fixed array inside the library instead.  This test calls
-it through the C ABI twice in a row and checks each result against the
+it through the C ABI three times in a row and checks each result against the
 regular entry point, which takes caller-allocated partial buffers; it also
 checks that a size beyond the built-in array is refused.
 
@@ -34,7 +34,9 @@ def test_noalloc_attention_matches_regular_entry_point(cuda, gpt2b):
     rng = np.random.default_rng(77)
     kv = torch.from_numpy(rng.standard_normal(2 * NH * maxT * hs, dtype=np.float32)).to("cuda", torch.bfloat16)
     stream = torch.cuda.current_stream().cuda_stream
-    for call, (pos, S) in enumerate([(700, 8), (1023, 13)]):  # two calls in a row, different sizes
+    # calls in a row with different sizes; the third has fewer splits than the second, so a
+    # merge that read a stale slot left by the previous call would change the output
+    for call, (pos, S) in enumerate([(700, 8), (1023, 13), (1023, 5)]):
         qkv = torch.from_numpy(rng.standard_normal(3 * NH * hs, dtype=np.float32)).to("cuda", torch.bfloat16)
         d_pos = torch.tensor([pos], dtype=torch.int32, device="cuda")
         # the regular entry point with caller-allocated partials
@@ -50,6 +52,8 @@ def test_noalloc_attention_matches_regular_entry_point(cuda, gpt2b):
         g, w = got.float().cpu().numpy(), want.float().cpu().numpy()
         assert np.isfinite(g).all(), call
         assert rel_err(g, w) < 1e-2, call  # the BF16 attention tolerance used by the other tests
+        # the same split and merge kernels on the same inputs: the outputs are bit-identical
+        assert torch.equal(got, want), call
 
 
 def test_noalloc_attention_refuses_sizes_beyond_its_array(cuda, gpt2b):
