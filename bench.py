@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""GPT-2 124M batch-1 greedy decode benchmark (ms/token) on B200.
+"""GPT-2 batch-1 greedy decode benchmark (ms/token) on B200.
 
 Workload (default ``--config bf16``): random-init
 GPT-2 124M (Linear/embedding N(0,0.02), wpe N(0,0.01), LN 1/0, biases 0;
@@ -7,12 +7,22 @@ numpy PCG64 seed 1234), BF16 weights/activations/KV, FP32 logits; a 24-token
 uniform-random prompt (seed 24) is fed once, then each *step* is the 1000
 greedy decode forwards at positions 24..1023 (restarting from the first
 generated token).  ``--config int8|fp8|f32`` selects the other precisions
-(INT8/FP8 use 8-bit KV).
+(INT8/FP8 use 8-bit KV) as the headline value.
 
-One JSON line on rank 0 (see the repository's measurement notes for field
-definitions).  ``--impl reference`` times the reference's CPU decode path
-(its own CPU loops compiled from source, oracle/_ref) on a bounded sample.
-With N > 1 GPUs (torchrun) each rank runs an independent replica (the 124M
+One JSON line on rank 0.  Besides the headline value it carries
+* ``precisions`` (1 GPU): INT8+KV8, FP8+KV8 and FP32 on the same workload;
+* ``xl_tp`` (every N): GPT-2-XL INT8 decode, tensor parallel over all launched
+  ranks (TP = N; configs[4]);
+* ``gemv`` (1 GPU): the config-0 GEMVs standalone, L2 cold and warm;
+* ``cpu_baseline`` (1 GPU): the reference's CPU loops on a bounded sample of
+  decode positions spread over 24..1023.
+
+``--impl reference`` times the reference's CPU decode path (its own CPU loops
+compiled from source, oracle/_ref) on a bounded sample, with every host core.
+``--config xl-int8`` prints the tensor-parallel GPT-2-XL line alone;
+``--config fp8-long`` times configs[3] (FP8 weights + FP8 KV at positions
+512..1023, attention split+merge with 8 splits against the single-CTA form).
+With N > 1 GPUs (torchrun) each rank runs an independent 124M replica (the 124M
 decode does not shard); the value is whole-job ms per token.
 """
 from __future__ import annotations
@@ -44,6 +54,10 @@ METRIC = "ms/token GPT-2 124M b=1 decode (FP32/BF16/INT8/FP8); GEMV GB/s vs HBM 
 # GPT-2-XL INT8 weights, BF16 KV, tensor parallel over the launched ranks (TP = N)
 XL_CONFIG = "xl-int8"
 XL_METRIC = "ms/token GPT-2-XL INT8 b=1 decode, tensor parallel over N GPUs"
+# FP8 weights + FP8 KV, positions 512..1023
+LONG_CONFIG = "fp8-long"
+LONG_METRIC = "ms/token GPT-2 124M FP8+FP8-KV decode at positions 512..1023; attention split+merge (S=8) vs fused_single"
+LONG_FIRST = 512
 
 
 def env_rank():
@@ -78,6 +92,13 @@ def algo_bytes_per_token(cfg, wmode, kvmode, first_pos=PROMPT_LEN, n=GEN):
     mean_len = first_pos + (n - 1) / 2.0 + 1.0
     kv = L * 2 * NH * mean_len * (hs * kvb + (4 if kvmode == "8bit" else 0))
     return float(b + kv)
+
+
+def spread_positions(n, first=PROMPT_LEN, last=PROMPT_LEN + GEN - 1):
+    """n decode positions evenly spread over first..last; their mean is the
+    workload's mean position, so a per-position cost that grows with the
+    context is sampled at its average."""
+    return [int(first + (last - first) * (i + 0.5) / n) for i in range(n)]
 
 
 class ClockSampler:
@@ -131,10 +152,22 @@ class ClockSampler:
                 "samples": len(sm), "power_w_max": max(power) if power else None}
 
 
+def quantize_image(img16, wmode):
+    """The library's quantize.cu-compatible quantiser on a v5 image."""
+    from cuda_gpt2_inference_b200 import check, lib
+    ob, ns = ctypes.c_size_t(), ctypes.c_size_t()
+    check(lib().gpt2b_quantized_size(img16, len(img16), ctypes.byref(ob), ctypes.byref(ns)))
+    out = ctypes.create_string_buffer(ob.value)
+    sc = np.zeros(ns.value, np.float32)
+    check(lib().gpt2b_quantize_buffer(img16, len(img16), out, sc.ctypes.data_as(ctypes.c_void_p),
+                                      1 if wmode == "fp8" else 0))
+    return out.raw, sc
+
+
 def make_model(wmode, kvmode, seed=1234):
     """Random-init 124M image in the reference format (8-bit: quantised with the
     library's quantize.cu-compatible quantiser)."""
-    from cuda_gpt2_inference_b200 import check, lib, weights
+    from cuda_gpt2_inference_b200 import weights
     cfg = weights.GPT2_124M
     params = weights.synth_params(cfg, seed, init="spec")
     if wmode == "f32":
@@ -142,18 +175,36 @@ def make_model(wmode, kvmode, seed=1234):
     img16 = weights.image(params, cfg, "bf16")
     if wmode == "bf16":
         return cfg, params, img16, None
-    ob, ns = ctypes.c_size_t(), ctypes.c_size_t()
-    check(lib().gpt2b_quantized_size(img16, len(img16), ctypes.byref(ob), ctypes.byref(ns)))
-    out = ctypes.create_string_buffer(ob.value)
-    sc = np.zeros(ns.value, np.float32)
-    check(lib().gpt2b_quantize_buffer(img16, len(img16), out, sc.ctypes.data_as(ctypes.c_void_p),
-                                      1 if wmode == "fp8" else 0))
-    return cfg, params, out.raw, sc
+    img, sc = quantize_image(img16, wmode)
+    return cfg, params, img, sc
+
+
+# --------------------------------------------------------------------------------------
+# standalone GEMVs
+# --------------------------------------------------------------------------------------
+def time_launches(fn, flush=None, reps=20, warm=5):
+    """Median CUDA-event time of fn() (ms).  Before each launch the GPU is kept
+    busy (an L2-sized fill for cold runs, a spin otherwise) while the host
+    queues the launch, so no host launch latency lands between the events."""
+    import torch
+    evs = []
+    for i in range(reps + warm):
+        if flush is not None:
+            flush.fill_(i & 0xFF)  # 512 MB > L2: the operands come from HBM
+        torch.cuda._sleep(200000)  # ~0.1 ms of spinning: the host gets ahead of the GPU
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        evs.append((s, e))
+    torch.cuda.synchronize()
+    return statistics.median(s.elapsed_time(e) for s, e in evs[warm:])
 
 
 def gemv_table(peak):
-    """Standalone decode GEMVs (config-0 shapes), L2 flushed before each
-    launch, CUDA-event median of 20: GB/s of algorithmic bytes."""
+    """Standalone decode GEMVs (config-0 shapes): GB/s of algorithmic bytes,
+    L2 flushed before each launch (cold) and with the operands L2-resident
+    (warm), CUDA-event median of 20 launches each."""
     import torch
 
     from cuda_gpt2_inference_b200 import ops
@@ -176,56 +227,97 @@ def gemv_table(peak):
                 out = torch.empty(M, device="cuda")
                 fn = lambda: ops.launch_GEMV6(out, W, x, M, K)  # noqa: E731
                 nbytes = (M * K + K) * W.element_size() + 4 * M
-            times = []
-            for i in range(25):
-                flush.fill_(i & 0xFF)
-                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                s.record()
-                fn()
-                e.record()
-                e.synchronize()
-                if i >= 5:
-                    times.append(s.elapsed_time(e))
-            ms = statistics.median(times)
-            gbs = nbytes / (ms * 1e-3) / 1e9
-            res[f"{dt}_{M}x{K}"] = {"us": round(ms * 1e3, 2), "GB/s": round(gbs, 1), "frac": round(gbs / peak, 3)}
+            fn()
+            cold = time_launches(fn, flush)
+            warm = time_launches(fn)
+            gbs = nbytes / (cold * 1e-3) / 1e9
+            res[f"{dt}_{M}x{K}"] = {"us": round(cold * 1e3, 2), "GB/s": round(gbs, 1), "frac": round(gbs / peak, 3),
+                                    "warm_us": round(warm * 1e3, 2),
+                                    "warm_GB/s": round(nbytes / (warm * 1e-3) / 1e9, 1), "bytes": nbytes}
     del flush
     return res
 
 
-def cpu_reference_decode(params, cfg, tokens_per_step, steps, warmup):
-    """The reference's CPU decode (its CPU loops, compiled from source)."""
-    import oracle
-    from cuda_gpt2_inference_b200 import weights
-    lib = oracle.ref_cpu("decode")
-    flat = np.concatenate([weights.bf16_to_f32(weights.bf16_bits(params[n])).ravel() for n in weights.NAMES])
-    flat = np.ascontiguousarray(flat, np.float32)
-    cfg6 = np.array([cfg["maxT"], cfg["V"], cfg["L"], cfg["NH"], cfg["C"], cfg["Vp"]], np.int32)
-    h = lib.ref_decoder_create(cfg6.ctypes.data_as(ctypes.c_void_p), flat.ctypes.data_as(ctypes.c_void_p))
-    rng = np.random.default_rng(24)
-    prompt = rng.integers(0, cfg["V"], PROMPT_LEN).astype(np.int32)
-    tok = int(prompt[0])
-    pos = 0
-    for _ in range(warmup):
-        tok = lib.ref_decoder_step(h, tok, pos, None)
-        pos += 1
-    t0 = time.perf_counter()
-    n = 0
-    for _ in range(steps):
-        for _ in range(tokens_per_step):
-            tok = lib.ref_decoder_step(h, tok, pos, None)
-            pos = pos + 1 if pos + 1 < cfg["maxT"] else PROMPT_LEN
-            n += 1
-    dt = time.perf_counter() - t0
-    lib.ref_decoder_free(h)
-    return dt * 1e3 / n, n
-
-
+# --------------------------------------------------------------------------------------
+# the reference's CPU decode (its own CPU loops compiled from source)
+# --------------------------------------------------------------------------------------
 def cores():
     try:
         return len(os.sched_getaffinity(0))
     except Exception:
         return os.cpu_count() or 1
+
+
+def flat_params_124m(params):
+    """The 16 tensors as FP32 (the BF16-rounded values the GPU engine holds)."""
+    from cuda_gpt2_inference_b200 import weights
+    flat = np.concatenate([weights.bf16_to_f32(weights.bf16_bits(params[n])).ravel() for n in weights.NAMES])
+    return np.ascontiguousarray(flat, np.float32)
+
+
+def flat_params_from_w8(img, sc, cfg):
+    """The 16 tensors of an 8-bit mixed image as FP32: the five Linear groups
+    dequantised (code x row scale), the rest widened from BF16."""
+    from cuda_gpt2_inference_b200 import weights
+    shp = weights.shapes(cfg)
+    total = sum(int(np.prod(v)) for v in shp.values())
+    flat = np.empty(total, np.float32)
+    buf = np.frombuffer(img, np.uint8)
+    off, foff, soff = 1024, 0, 0
+    for name in weights.NAMES:
+        n = int(np.prod(shp[name]))
+        if name in weights.LINEAR:
+            rows = n // cfg["C"] if name != "fcprojw" else n // (4 * cfg["C"])
+            codes = buf[off:off + n].view(np.int8).reshape(rows, -1)
+            s = sc[soff:soff + rows]
+            for r0 in range(0, rows, 8192):  # chunks keep the temporaries small
+                flat[foff + r0 * codes.shape[1]: foff + (r0 + codes[r0:r0 + 8192].shape[0]) * codes.shape[1]] = \
+                    (codes[r0:r0 + 8192].astype(np.float32) * s[r0:r0 + 8192, None]).ravel()
+            off += n
+            soff += rows
+        else:
+            flat[foff:foff + n] = weights.bf16_to_f32(buf[off:off + 2 * n].view(np.uint16))
+            off += 2 * n
+        foff += n
+    return flat
+
+
+class CpuDecoder:
+    """The reference's CPU decode path over all host cores."""
+
+    def __init__(self, flat, cfg):
+        import oracle
+        self.lib = oracle.ref_cpu("decode")
+        # torchrun sets OMP_NUM_THREADS=1 for its ranks: the reference path gets every core
+        self.threads = int(self.lib.ref_set_threads(cores()))
+        self.flat = flat
+        self.cfg6 = np.array([cfg["maxT"], cfg["V"], cfg["L"], cfg["NH"], cfg["C"], cfg["Vp"]], np.int32)
+        self.h = self.lib.ref_decoder_create(self.cfg6.ctypes.data_as(ctypes.c_void_p),
+                                             flat.ctypes.data_as(ctypes.c_void_p))
+
+    def time_positions(self, positions):
+        """ms per forward over the given positions (the timing sample; the
+        attention cost of a position is the same whatever the cached rows hold)."""
+        t0 = time.perf_counter()
+        for p in positions:
+            self.lib.ref_decoder_step(self.h, 1 + p % 97, p, None)
+        return (time.perf_counter() - t0) * 1e3 / len(positions)
+
+    def close(self):
+        self.lib.ref_decoder_free(self.h)
+
+
+def cpu_baseline_124m(params, cfg, budget_s=15.0):
+    dec = CpuDecoder(flat_params_124m(params), cfg)
+    dec.time_positions([PROMPT_LEN])  # warm-up
+    probe = dec.time_positions(spread_positions(2))
+    n = int(max(4, min(64, budget_s * 1e3 / max(probe, 1e-3))))
+    ms = dec.time_positions(spread_positions(n))
+    dec.close()
+    return {"value": round(ms, 3), "unit": "ms/token", "cores": dec.threads, "kind": "reference",
+            "sample": f"{n} decode forwards of the same model by the reference CPU loops (FP32 math on the BF16 "
+                      f"weights) at positions spread evenly over {PROMPT_LEN}..{PROMPT_LEN + GEN - 1} "
+                      f"(mean {np.mean(spread_positions(n)):.1f})"}
 
 
 def run_reference(args, rank, world):
@@ -236,27 +328,125 @@ def run_reference(args, rank, world):
     if not oracle.ref_available("libref_cpu_decode.so"):
         print(json.dumps({"impl": "reference", "unavailable": "reference CPU loops were not built (oracle/_ref)"}))
         return 0
-    cfg = weights.GPT2_124M
-    params = weights.synth_params(cfg, 1234, init="spec")
-    # one probe token to size the sample so the whole run stays within minutes
-    probe_ms, _ = cpu_reference_decode(params, cfg, 1, 1, 0)
-    per_step = int(max(1, min(16, 8000.0 / max(probe_ms, 1e-3) / max(1, args.steps))))
-    ms, n = cpu_reference_decode(params, cfg, per_step, args.steps, args.warmup)
-    c = cores()
-    sample = (f"{per_step} decode tokens per step from position 0 (prompt then greedy), "
-              f"FP32 math on the BF16 weights, {n} tokens timed")
+    if args.config == XL_CONFIG:
+        cfg, img, sc = xl_model(0, 1)
+        flat = flat_params_from_w8(img, sc, cfg)
+        del img
+        metric, dtype = XL_METRIC, "f32"
+        wl = "gpt2-xl greedy decode (int8 weights dequantised to FP32), CPU reference loops"
+        what = "FP32 math on the dequantised INT8 weights"
+        par = f"reference CPU path (tp{world} on the GPU arm)"
+    else:
+        cfg = weights.GPT2_124M
+        wmode, kvmode = CONFIGS.get(args.config, ("bf16", "floatx"))
+        if wmode in ("int8", "fp8"):
+            _, _, img, sc = make_model(wmode, kvmode)
+            flat = flat_params_from_w8(img, sc, cfg)
+            what = f"FP32 math on the dequantised {wmode.upper()} weights"
+        else:
+            flat = flat_params_124m(weights.synth_params(cfg, 1234, init="spec"))
+            what = "FP32 math on the BF16 weights"
+        metric, dtype = METRIC, "f32"
+        wl = "gpt2-124m greedy decode, CPU reference loops"
+        par = "replicas"
+    dec = CpuDecoder(flat, cfg)
+    dec.time_positions([PROMPT_LEN])
+    probe = dec.time_positions(spread_positions(2))
+    # tokens per step sized so the whole --steps/--warmup run stays within a few minutes
+    per_step = int(max(1, min(16, 8000.0 / max(probe, 1e-3) / max(1, args.steps))))
+    pos = spread_positions(per_step)
+    for _ in range(args.warmup):
+        dec.time_positions(pos[:1])
+    ms_steps = [dec.time_positions(pos) for _ in range(args.steps)]
+    dec.close()
+    ms = float(np.mean(ms_steps))
+    sample = (f"{per_step} decode forwards per step at positions spread evenly over {PROMPT_LEN}.."
+              f"{PROMPT_LEN + GEN - 1}, {what}, {per_step * args.steps} forwards timed")
     line = {
-        "impl": "reference", "metric": METRIC, "value": round(ms, 3), "unit": "ms/token", "n_gpus": world,
+        "impl": "reference", "metric": metric, "value": round(ms, 3), "unit": "ms/token", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms * per_step, 3),
-        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "gpt2-124m greedy decode, CPU reference loops", "seq_len": cfg["maxT"],
-                   "prompt": PROMPT_LEN, "parallelism": "replicas"},
-        "cpu_baseline": {"value": round(ms, 3), "unit": "ms/token", "cores": c, "kind": "reference",
+        "higher_is_better": False, "scaling": "weak" if par == "replicas" else "strong", "vs_baseline": None,
+        "dtype": dtype, "data": "synthetic",
+        "config": {"workload": wl, "seq_len": cfg["maxT"], "prompt": PROMPT_LEN, "parallelism": par},
+        "cpu_baseline": {"value": round(ms, 3), "unit": "ms/token", "cores": dec.threads, "kind": "reference",
                          "sample": sample},
         "e2e": {"value": round(ms, 3), "unit": "ms/token", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
     return 0
+
+
+# --------------------------------------------------------------------------------------
+# the GPU engine
+# --------------------------------------------------------------------------------------
+def measure_engine(eng, prompt, steps, warmup, world=1, clocks=None, local_rank=0):
+    """Device ms/token of `steps` decode calls of GEN tokens from position 24
+    (max over ranks), then the end-to-end generate() through the C ABI with
+    host buffers (wall clock, max over ranks)."""
+    import torch
+    import torch.distributed as dist
+    first, _ = eng.generate(prompt, 0)  # prefill: 24 teacher-forced forwards
+    g0 = int(first[0])
+    stream = torch.cuda.ExternalStream(eng.stream)
+
+    def step():
+        eng.set_position(g0, PROMPT_LEN)
+        eng.decode(GEN)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local_rank) if clocks else None
+    if sampler:
+        sampler.start()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        step()
+    end.record(stream)
+    end.synchronize()
+    torch.cuda.synchronize()
+    clk = sampler.stop() if sampler else None
+    if world > 1:
+        dist.barrier()
+    t = torch.tensor([start.elapsed_time(end)], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    decoded = eng.history(PROMPT_LEN, GEN + 1)
+    e2e_tokens, _ = eng.generate(prompt, GEN)  # also warms the host API path before timing it
+    deterministic = bool(np.array_equal(decoded, e2e_tokens))
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        eng.generate(prompt, GEN)
+    te = torch.tensor([(time.perf_counter() - t0) * 1e3], device="cuda")
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    return {"max_ms": max_ms, "ms_per_token": max_ms / (steps * GEN), "e2e_ms_per_token": float(te.item()) / (steps * GEN),
+            "deterministic": deterministic, "clocks": clk}
+
+
+def precision_block(wmode, kvmode, steps, warmup, peak, prompt):
+    """One precision on the same workload (1 GPU, persistent kernel)."""
+    from cuda_gpt2_inference_b200.engine import Engine
+    cfg, _, img, sc = make_model(wmode, kvmode)
+    eng = Engine.from_buffer(img, wmode, kvmode, sc)
+    del img
+    r = measure_engine(eng, prompt, steps, warmup)
+    kps = eng.kernels_per_step()
+    eng.close()
+    ab = algo_bytes_per_token(cfg, wmode, kvmode)
+    ach = ab / (r["ms_per_token"] * 1e-3) / 1e9
+    return {"weights": wmode, "kv": "8-bit" if kvmode == "8bit" else wmode, "ms_per_token": round(r["ms_per_token"], 5),
+            "e2e_ms_per_token": round(r["e2e_ms_per_token"], 5), "algorithmic_bytes_per_token": int(ab),
+            "achieved_GB/s": round(ach, 1), "frac": round(ach / peak, 4), "steps": steps, "warmup": warmup,
+            "deterministic": r["deterministic"],
+            "kernel": "persistent cooperative kernel" if kps == 0 else f"{kps} kernels per step"}
 
 
 def run_ours(args, rank, local_rank, world):
@@ -275,58 +465,12 @@ def run_ours(args, rank, local_rank, world):
     if args.path == "kernels":
         eng.set_option(pkg.OPT_PERSISTENT, 0)
     kps = eng.kernels_per_step()  # 0: persistent kernel, one launch per decode call
-    rng = np.random.default_rng(24)
-    prompt = rng.integers(0, cfg["V"], PROMPT_LEN).astype(np.int32)
-    first, _ = eng.generate(prompt, 0)  # prefill: 24 teacher-forced forwards
-    g0 = int(first[0])
-    stream = torch.cuda.ExternalStream(eng.stream)
-
-    def step():
-        eng.set_position(g0, PROMPT_LEN)
-        eng.decode(GEN)
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    clocks = ClockSampler(local_rank)
-    clocks.start()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    for _ in range(args.steps):
-        step()
-    end.record(stream)
-    end.synchronize()
-    torch.cuda.synchronize()
-    clk = clocks.stop()
-    if world > 1:
-        dist.barrier()
-    total_ms = start.elapsed_time(end)
-    t = torch.tensor([total_ms], device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    max_ms = float(t.item())
-    per_replica = max_ms / (args.steps * GEN)
+    prompt = np.random.default_rng(24).integers(0, cfg["V"], PROMPT_LEN).astype(np.int32)
+    r = measure_engine(eng, prompt, args.steps, args.warmup, world, clocks=True, local_rank=local_rank)
+    max_ms = r["max_ms"]
+    per_replica = r["ms_per_token"]
     value = max_ms / (args.steps * GEN * world)
-    # determinism check: the timed device-resident decode and the host API agree
-    decoded = eng.history(PROMPT_LEN, GEN + 1)
-    e2e_tokens, _ = eng.generate(prompt, GEN)  # also warms the host API path before timing it
-    deterministic = bool(np.array_equal(decoded, e2e_tokens))
-
-    # end to end through the C ABI with host buffers (prompt H2D, tokens D2H)
-    if world > 1:
-        dist.barrier()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        eng.generate(prompt, GEN)
-    e2e_ms = (time.perf_counter() - t0) * 1e3
-    te = torch.tensor([e2e_ms], device="cuda")
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = float(te.item()) / (args.steps * GEN * world)
+    e2e_value = r["e2e_ms_per_token"] / world
 
     peak, peak_kind = measured_peaks()
     abytes = algo_bytes_per_token(cfg, wmode, kvmode)
@@ -356,28 +500,40 @@ def run_ours(args, rank, local_rank, world):
                                "whole decode loop (persistent cooperative kernel, 1 launch per %d steps)" % GEN,
                      "algorithmic_bytes_per_token": int(abytes), "peak_kind": peak_kind},
         "gpu_launches": kps * GEN * args.steps if kps else args.steps,
-        "clocks": clk,
-        "deterministic": deterministic,
+        "clocks": r["clocks"],
+        "deterministic": r["deterministic"],
     }
-    if rank == 0 and world == 1 and not args.quick:
+    eng.close()
+    del img
+    extras = world == 1 and not args.quick
+    if extras:
+        # the other precisions on the same workload (a few steps each)
+        line["precisions"] = {}
+        for name, (wm, kv) in CONFIGS.items():
+            if name == args.config:
+                continue
+            try:
+                line["precisions"][name] = precision_block(wm, kv, min(args.steps, 5), 3, peak, prompt)
+            except Exception as ex:
+                line["precisions"][name] = {"error": str(ex)[:200]}
         try:
             line["gemv"] = gemv_table(peak)
         except Exception as ex:  # optional extra; never fail the bench line for it
             line["gemv"] = {"error": str(ex)[:200]}
         try:
-            ms, n = cpu_reference_decode(params, cfg, 2, 2, 1)
-            n_tok = int(max(2, min(64, 15000.0 / max(ms, 1e-3))))
-            ms, n = cpu_reference_decode(params, cfg, n_tok, 1, 0)
-            line["cpu_baseline"] = {"value": round(ms, 3), "unit": "ms/token", "cores": cores(), "kind": "reference",
-                                    "sample": f"{n} tokens of the same model decoded by the reference CPU loops "
-                                              f"(FP32 math on the BF16 weights), from position 0"}
+            line["cpu_baseline"] = cpu_baseline_124m(params, cfg)
         except Exception as ex:
             line["cpu_baseline"] = {"error": str(ex)[:200]}
         try:
-            line["reference_kernels_b200"] = reference_cuda_engine(img, sc, wmode, kvmode)
+            line["reference_kernels_b200"] = reference_cuda_engine(*make_model(wmode, kvmode)[2:], wmode, kvmode)
         except Exception as ex:
             line["reference_kernels_b200"] = {"error": str(ex)[:200]}
-    eng.close()
+    if not args.no_xl:
+        # GPT-2-XL INT8 tensor parallel over every launched rank (TP = N), every N
+        try:
+            line["xl_tp"] = xl_tp_block(args, rank, local_rank, world, own_group=False)
+        except Exception as ex:
+            line["xl_tp"] = {"error": str(ex)[:300]}
     if rank == 0:
         print(json.dumps(line))
     if world > 1:
@@ -415,123 +571,199 @@ def reference_cuda_engine(img, sc, wmode, kvmode):
             "what": "reference inference_gpt2_opt graph loop compiled for sm_100a, wall ms / 999 tokens"}
 
 
+# --------------------------------------------------------------------------------------
+# GPT-2-XL tensor parallel
+# --------------------------------------------------------------------------------------
 def xl_model(rank, world):
     """GPT-2-XL INT8 image + scales (random init, spec), generated once by rank 0
     into /dev/shm and read by every rank."""
-    import torch.distributed as dist
-
-    from cuda_gpt2_inference_b200 import check, lib, weights
+    from cuda_gpt2_inference_b200 import weights
     cfg = weights.GPT2_XL
     base = "/dev/shm/gpt2b_xl_int8_s1234"
     if rank == 0 and not os.path.exists(base + ".ok"):
         img16 = weights.image_stream(cfg, 1234, "spec", "bf16")
-        ob, ns = ctypes.c_size_t(), ctypes.c_size_t()
-        check(lib().gpt2b_quantized_size(img16, len(img16), ctypes.byref(ob), ctypes.byref(ns)))
-        out = ctypes.create_string_buffer(ob.value)
-        sc = np.zeros(ns.value, np.float32)
-        check(lib().gpt2b_quantize_buffer(img16, len(img16), out, sc.ctypes.data_as(ctypes.c_void_p), 0))
+        out, sc = quantize_image(img16, "int8")
         del img16
         with open(base + ".bin", "wb") as f:
-            f.write(out.raw)
+            f.write(out)
         sc.tofile(base + "_scales.bin")
         open(base + ".ok", "w").close()
     if world > 1:
+        import torch.distributed as dist
         dist.barrier()
     with open(base + ".bin", "rb") as f:
         img = f.read()
     return cfg, img, np.fromfile(base + "_scales.bin", dtype=np.float32)
 
 
-def run_xl_tp(args, rank, local_rank, world):
+def xl_tp_block(args, rank, local_rank, world, own_group):
     """GPT-2-XL INT8 (BF16 KV), batch 1, 1000 greedy steps after a 24-token
-    prompt, tensor parallel over the WORLD_SIZE ranks (one engine per GPU,
-    NCCL all-reduces of the row-parallel projections)."""
-    import torch
-    import torch.distributed as dist
-
+    prompt, tensor parallel over the WORLD_SIZE ranks (one engine per GPU; the
+    persistent kernel with peer stores between the ranks, or the per-kernel
+    path with NCCL all-reduces for --path kernels).  Collective over the ranks;
+    returns the block on every rank."""
     from cuda_gpt2_inference_b200 import tp
     from cuda_gpt2_inference_b200.engine import Engine
-    torch.cuda.set_device(local_rank)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
-                                device_id=torch.device("cuda", local_rank))
     cfg, img, sc = xl_model(rank, world)
+    p2p = args.path == "persistent"
     if world > 1:
-        eng = tp.engine(img, "int8", "floatx", sc, rank, world, tp.shared_group_id(rank),
-                        p2p=(args.path == "persistent"))
+        eng = tp.engine(img, "int8", "floatx", sc, rank, world, tp.shared_group_id(rank), p2p=p2p)
     else:
         eng = Engine.from_buffer(img, "int8", "floatx", sc)
     del img
     kps = eng.kernels_per_step()
+    steps, warmup = (args.steps, args.warmup) if own_group else (min(args.steps, 5), 3)
     prompt = np.random.default_rng(24).integers(0, cfg["V"], PROMPT_LEN).astype(np.int32)
-    first, _ = eng.generate(prompt, 0)
-    g0 = int(first[0])
-    stream = torch.cuda.ExternalStream(eng.stream)
-
-    def step():
-        eng.set_position(g0, PROMPT_LEN)
-        eng.decode(GEN)
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    clocks = ClockSampler(local_rank)
-    clocks.start()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    for _ in range(args.steps):
-        step()
-    end.record(stream)
-    end.synchronize()
-    clk = clocks.stop()
-    t = torch.tensor([start.elapsed_time(end)], device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    max_ms = float(t.item())
-    value = max_ms / (args.steps * GEN)
-    decoded = eng.history(PROMPT_LEN, GEN + 1)
-    e2e_tokens, _ = eng.generate(prompt, GEN)
-    if world > 1:
-        dist.barrier()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        eng.generate(prompt, GEN)
-    te = torch.tensor([(time.perf_counter() - t0) * 1e3], device="cuda")
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = float(te.item()) / (args.steps * GEN)
+    r = measure_engine(eng, prompt, steps, warmup, world, clocks=own_group, local_rank=local_rank)
+    eng.close()
     peak, peak_kind = measured_peaks()
     abytes = algo_bytes_per_token(cfg, "int8", "floatx")
-    achieved = abytes / world / (value * 1e-3) / 1e9  # per GPU: each rank reads ~1/TP of the bytes
+    per_gpu = abytes / world / (r["ms_per_token"] * 1e-3) / 1e9  # each rank reads ~1/TP of the bytes
+    exchange = ("single gpu, persistent kernel" if world == 1 and kps == 0 else
+                "single gpu, per-kernel path" if world == 1 else
+                "persistent kernel per rank, row-parallel partials stored into every rank's memory over NVLink"
+                if kps == 0 else f"per-kernel path, NCCL all-reduce after each row-parallel GEMV ({2 * cfg['L']} "
+                                 f"per token) + all-gather of the LM picks")
+    return {"tp": world, "ms_per_token": round(r["ms_per_token"], 5),
+            "e2e_ms_per_token": round(r["e2e_ms_per_token"], 5),
+            "per_gpu_GB/s": round(per_gpu, 1), "frac": round(per_gpu / peak, 4), "peak": peak,
+            "peak_kind": peak_kind, "algorithmic_bytes_per_token": int(abytes), "exchange": exchange,
+            "steps": steps, "warmup": warmup, "deterministic": r["deterministic"], "clocks": r["clocks"],
+            "workload": "gpt2-xl b=1 greedy decode, int8 weights, bf16 kv, 1000 steps after a 24-token prompt "
+                        "(positions 24..1023)"}
+
+
+def run_xl_tp(args, rank, local_rank, world):
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
+                                device_id=torch.device("cuda", local_rank))
+    b = xl_tp_block(args, rank, local_rank, world, own_group=True)
     line = {
-        "metric": XL_METRIC, "value": round(value, 5), "unit": "ms/token", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(max_ms / args.steps, 3), "higher_is_better": False,
+        "metric": XL_METRIC, "value": b["ms_per_token"], "unit": "ms/token", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(b["ms_per_token"] * GEN, 3), "higher_is_better": False,
         "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": "gpt2-xl b=1 greedy decode, int8 weights, bf16 kv, 1000 steps after a 24-token "
-                               "prompt (positions 24..1023)",
-                   "model": "gpt2-xl (random init)", "global_batch": 1, "seq_len": cfg["maxT"],
+        "config": {"workload": b["workload"], "model": "gpt2-xl (random init)", "global_batch": 1, "seq_len": 1024,
                    "parallelism": f"tp{world}", "l2": "inputs larger than L2 (~1.7 GB per token)"},
-        "e2e": {"value": round(e2e_value, 5), "unit": "ms/token", "h2d_bytes_per_step": PROMPT_LEN * 4 + 12,
+        "e2e": {"value": b["e2e_ms_per_token"], "unit": "ms/token", "h2d_bytes_per_step": PROMPT_LEN * 4 + 12,
                 "d2h_bytes_per_step": (GEN + 1) * 4},
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
-                     "kernel": ("whole decode step per rank (%d kernels + %d NCCL collectives)" % (
-                         kps, 2 * cfg["L"] + 1 if world > 1 else 0)) if kps else
-                               "persistent kernel per rank, peer stores between ranks (1 launch per %d steps)" % GEN,
-                     "algorithmic_bytes_per_token": int(abytes)},
-        "gpu_launches": kps * GEN * args.steps if kps else args.steps,
-        "clocks": clk,
-        "deterministic": bool(np.array_equal(decoded, e2e_tokens)),
+        "roofline": {"bound": "hbm", "achieved": b["per_gpu_GB/s"], "peak": b["peak"], "unit": "GB/s",
+                     "frac": b["frac"], "traffic": None, "peak_kind": b["peak_kind"], "kernel": b["exchange"],
+                     "algorithmic_bytes_per_token": b["algorithmic_bytes_per_token"]},
+        "gpu_launches": args.steps, "clocks": b["clocks"], "deterministic": b["deterministic"],
     }
-    eng.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line))
+    return 0
+
+
+# --------------------------------------------------------------------------------------
+# configs[3]: FP8 weights + FP8 KV at positions 512..1023
+# --------------------------------------------------------------------------------------
+def run_fp8_long(args):
+    """Attention: 12 heads x 64, FP8 KV holding per-row quantised N(0,1) values,
+    q N(0,1); every position 512..1023 timed with split+merge (8 splits) and
+    with the single-CTA-per-head form (L2 flushed before each launch).  Whole
+    model: the FP8+KV8 engine decoding positions 512..1023."""
+    import torch
+
+    import cuda_gpt2_inference_b200 as pkg
+    from cuda_gpt2_inference_b200 import ops
+    from cuda_gpt2_inference_b200.engine import Engine
+    torch.cuda.set_device(0)
+    peak, peak_kind = measured_peaks()
+    NH, hs, maxT, S = 12, 64, 1024, 8
+    rng = np.random.default_rng(3)
+    # the FP8 KV cache, written row by row by the library's KV append (amax/448 per row)
+    cache = torch.zeros(2 * NH * maxT * hs, dtype=torch.uint8, device="cuda")
+    kvsc = torch.zeros(2 * NH * maxT, device="cuda")
+    qkv_all = torch.from_numpy(rng.standard_normal((maxT, 3 * NH * hs), dtype=np.float32)).to("cuda", torch.bfloat16)
+    d_pos = torch.arange(maxT, dtype=torch.int32, device="cuda")
+    for p in range(maxT):
+        ops.kv_cache_write(cache, qkv_all[p], 1, NH, hs, maxT, d_pos[p:p + 1], kv_scale=kvsc, fmt="fp8")
+    torch.cuda.synchronize()
+    po = torch.empty(NH * S * hs, device="cuda")
+    pl, pm = torch.empty(NH * S, device="cuda"), torch.empty(NH * S, device="cuda")
+    out = torch.empty(NH * hs, device="cuda", dtype=torch.bfloat16)
+    flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    positions = list(range(LONG_FIRST, maxT))
+    res = {}
+    for name in ("split8", "single"):
+        total_ms = 0.0
+        for p in positions:
+            q, dp = qkv_all[p], d_pos[p:p + 1]
+            if name == "split8":
+                fn = lambda: ops.attention_forward_kv_large(out, q, cache, 1, NH, hs, maxT, dp, po, pl, pm, S,  # noqa
+                                                            kv_scale=kvsc, fmt="fp8")
+            else:
+                fn = lambda: ops.attention_forward_kv_small(out, q, cache, 1, NH, hs, maxT, dp, kv_scale=kvsc,  # noqa
+                                                            fmt="fp8")
+            total_ms += time_launches(fn, flush, reps=3, warm=1)
+        mean_ms = total_ms / len(positions)
+        kv_bytes = float(np.mean([2 * NH * (p + 1) * (hs + 4) for p in positions]))
+        gbs = kv_bytes / (mean_ms * 1e-3) / 1e9
+        res[name] = {"us_per_call": round(mean_ms * 1e3, 3), "kv_bytes_mean": int(kv_bytes),
+                     "GB/s": round(gbs, 1), "frac": round(gbs / peak, 4)}
+    del flush
+    # whole model: FP8 weights + FP8 KV, decoding positions 512..1023
+    cfg, _, img, sc = make_model("fp8", "8bit")
+    eng = Engine.from_buffer(img, "fp8", "8bit", sc)
+    prompt = np.random.default_rng(24).integers(0, cfg["V"], PROMPT_LEN).astype(np.int32)
+    first, _ = eng.generate(prompt, 0)
+    eng.decode(LONG_FIRST - PROMPT_LEN)  # the cache up to position 511
+    tok512 = int(eng.history(LONG_FIRST, 1)[0])
+    n = maxT - LONG_FIRST
+    stream = torch.cuda.ExternalStream(eng.stream)
+    engines = {}
+    for path in ("persistent", "kernels"):
+        eng.set_option(pkg.OPT_PERSISTENT, 1 if path == "persistent" else 0)
+        if path == "kernels":
+            eng.set_option(pkg.OPT_SPLITS, S)
+
+        def step():
+            eng.set_position(tok512, LONG_FIRST)
+            eng.decode(n)
+
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        clocks = ClockSampler(0)
+        clocks.start()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        for _ in range(args.steps):
+            step()
+        e.record(stream)
+        e.synchronize()
+        clk = clocks.stop()
+        ms = s.elapsed_time(e) / (args.steps * n)
+        ab = algo_bytes_per_token(cfg, "fp8", "8bit", first_pos=LONG_FIRST, n=n)
+        engines[path] = {"ms_per_token": round(ms, 5), "achieved_GB/s": round(ab / (ms * 1e-3) / 1e9, 1),
+                         "frac": round(ab / (ms * 1e-3) / 1e9 / peak, 4), "algorithmic_bytes_per_token": int(ab),
+                         "clocks": clk,
+                         "attention": "persistent kernel: 12 splits per head" if path == "persistent" else
+                                      f"per-kernel path: {S} splits per head, merge in the projection prologue"}
+    eng.close()
+    line = {
+        "metric": LONG_METRIC, "value": engines["persistent"]["ms_per_token"], "unit": "ms/token", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(engines["persistent"]["ms_per_token"] * n, 3),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "fp8", "data": "synthetic",
+        "config": {"workload": "gpt2-124m fp8 weights + fp8 kv, greedy decode at positions 512..1023; attention "
+                               "12 heads x 64 over fp8 kv of N(0,1) values, q N(0,1)", "seq_len": maxT,
+                   "l2": "attention: flushed before each launch; model: inputs larger than L2"},
+        "roofline": {"bound": "hbm", "achieved": engines["persistent"]["achieved_GB/s"], "peak": peak,
+                     "unit": "GB/s", "frac": engines["persistent"]["frac"], "traffic": None, "peak_kind": peak_kind,
+                     "kernel": "whole decode loop (persistent cooperative kernel)"},
+        "engine": engines, "attention_kernels": res,
+        "split8_vs_single": round(res["single"]["us_per_call"] / res["split8"]["us_per_call"], 3),
+        "gpu_launches": args.steps,
+    }
+    print(json.dumps(line))
     return 0
 
 
@@ -565,21 +797,29 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS) + [XL_CONFIG], default="bf16")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + [XL_CONFIG, LONG_CONFIG], default="bf16")
     ap.add_argument("--path", choices=["persistent", "kernels"], default="persistent",
                     help="decode step implementation (persistent falls back to kernels where unsupported)")
-    ap.add_argument("--quick", action="store_true", help="skip the optional extras (GEMV table, CPU and reference bars)")
+    ap.add_argument("--quick", action="store_true",
+                    help="skip the 1-GPU extras (other precisions, GEMV table, CPU and reference bars)")
+    ap.add_argument("--no-xl", action="store_true", help="skip the GPT-2-XL tensor-parallel block")
     ap.add_argument("--profile-case", action="store_true",
                     help="small case for profilers: prefill, decode to position 500, then one 8-step decode "
                          "(the 3rd engine launch); prints no bench line")
     args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
     rank, local_rank, world = env_rank()
     if args.profile_case:
         return run_profile_case(args)
-    if args.config == XL_CONFIG and args.impl == "ours":
-        return run_xl_tp(args, rank, local_rank, world)
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.config == XL_CONFIG:
+        return run_xl_tp(args, rank, local_rank, world)
+    if args.config == LONG_CONFIG:
+        if rank != 0:
+            return 0
+        return run_fp8_long(args)
     return run_ours(args, rank, local_rank, world)
 
 

@@ -34,7 +34,9 @@ ERR_CUDA = 2000
 # weight / KV modes
 W_F32, W_BF16, W_INT8, W_FP8 = 0, 1, 2, 3
 KV_FLOATX, KV_8BIT = 0, 1
-OPT_USE_GRAPH, OPT_USE_PDL, OPT_SPLITS, OPT_STEPS_PER_GRAPH, OPT_PERSISTENT = 1, 2, 3, 4, 5
+OPT_USE_GRAPH, OPT_USE_PDL, OPT_SPLITS, OPT_STEPS_PER_GRAPH, OPT_PERSISTENT, OPT_POLL_LIMIT = 1, 2, 3, 4, 5, 6
+# device error codes (gpt2b_device_error)
+DEVERR_GRID_TIMEOUT = 5
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int

@@ -953,6 +953,10 @@ int gpt2b_engine_set_option(gpt2b_engine* e, int option, int value) {
             if (value && !e->persist_ok) return GPT2B_ERR_UNSUPPORTED;  // (tensor parallel: connect first)
             e->use_persistent = value != 0;
             break;
+        case GPT2B_OPT_POLL_LIMIT:
+            if (value < 1024) return GPT2B_ERR_INVALID_ARG;
+            e->pp.poll_limit = (uint32_t)value;
+            break;
         default: return GPT2B_ERR_INVALID_ARG;
     }
     return GPT2B_OK;

@@ -130,6 +130,7 @@ struct PersistParams {
     int n_prompt = 0;
     unsigned* d_epoch = nullptr;  // advanced by n_steps per call
     int* abort_flag = nullptr;    // zero at launch
+    uint32_t poll_limit = 1u << 22;  // polls of one exchange wait before it gives up (GPT2B_OPT_POLL_LIMIT)
     float* logits = nullptr;      // Vp floats of the last step
     int n_steps = 0;
 };

@@ -65,9 +65,9 @@ constexpr int kNarrowKvRows = 96;     // and stage at most 96 positions per atte
 constexpr int kHSz = 64;              // head size
 constexpr int kMaxSplits = 32;        // attention splits per head
 constexpr int kMiscFloats = 128;      // reduction scratch, new-row codes and scales, stop flag
+constexpr int kXmaxSlot = 104;        // misc[104..111]: per-warp max |x| of a phase (8-bit tensor-core stages)
 constexpr int kGatherJ = 32;          // exchange words per consumer thread and gather (4C <= 8192)
 constexpr int kGatherJs = 16;         // the short gather (n <= 4096 words)
-constexpr uint32_t kPollLimit = 1u << 22;
 enum { kPhQkv = 0, kPhProj = 1, kPhFc = 2, kPhFcproj = 3, kPhLm = 4 };
 
 // Phase timeline for profiling builds (-DGPT2B_PERSIST_TRACE): consumer
@@ -162,7 +162,7 @@ __device__ __noinline__ void give_up(int* flag, const PeerSet* ps) {
 // Words i = tid + j*kCT (i < n, j < J) of src into out[j]; all loads of a
 // round are in flight together.  False on timeout (recorded) or abort.
 template <int J, bool SYS>
-__device__ __noinline__ bool ll_gather_j(int* abort_flag, const PeerSet* ps, const unsigned long long* src, int n,
+__device__ __noinline__ bool ll_gather_j(int* abort_flag, const PeerSet* ps, uint32_t plim, const unsigned long long* src, int n,
                                          uint32_t tag,
                                          float* out) {
     const int tid = threadIdx.x;
@@ -182,7 +182,7 @@ __device__ __noinline__ bool ll_gather_j(int* abort_flag, const PeerSet* ps, con
                 pending &= ~(1u << j);
             }
         if (!pending) break;
-        if (it > kPollLimit) { give_up(abort_flag, ps); return false; }
+        if (it > plim) { give_up(abort_flag, ps); return false; }
         if ((it & 15) == 15 && aborted(abort_flag)) return false;
         __nanosleep(32);
     }
@@ -192,7 +192,7 @@ __device__ __noinline__ bool ll_gather_j(int* abort_flag, const PeerSet* ps, con
 // 16-byte poll per pair (half the requests of word polls; src 16-byte aligned).  False on
 // timeout (recorded) or abort.
 template <int J2, bool SYS>
-__device__ __noinline__ bool ll_gather2_j(int* abort_flag, const PeerSet* ps, const unsigned long long* src, int n,
+__device__ __noinline__ bool ll_gather2_j(int* abort_flag, const PeerSet* ps, uint32_t plim, const unsigned long long* src, int n,
                                           uint32_t tag, float* out) {
     const int tid = threadIdx.x;
     uint32_t pending = 0;
@@ -223,18 +223,18 @@ __device__ __noinline__ bool ll_gather2_j(int* abort_flag, const PeerSet* ps, co
                 pending &= ~(1u << j);
             }
         if (!pending) break;
-        if (it > kPollLimit) { give_up(abort_flag, ps); return false; }
+        if (it > plim) { give_up(abort_flag, ps); return false; }
         if ((it & 15) == 15 && aborted(abort_flag)) return false;
         __nanosleep(32);
     }
     return true;
 }
 template <bool WIDE>
-__device__ __forceinline__ bool ll_gather2(int* abort_flag, const PeerSet* ps, const unsigned long long* src, int n,
+__device__ __forceinline__ bool ll_gather2(int* abort_flag, const PeerSet* ps, uint32_t plim, const unsigned long long* src, int n,
                                            uint32_t tag, float* out) {
-    if constexpr (!WIDE) return ll_gather2_j<kGatherJs / 2, false>(abort_flag, ps, src, n, tag, out);
-    return n <= kGatherJs * kCT ? ll_gather2_j<kGatherJs / 2, false>(abort_flag, ps, src, n, tag, out)
-                                : ll_gather2_j<kGatherJ / 2, false>(abort_flag, ps, src, n, tag, out);
+    if constexpr (!WIDE) return ll_gather2_j<kGatherJs / 2, false>(abort_flag, ps, plim, src, n, tag, out);
+    return n <= kGatherJs * kCT ? ll_gather2_j<kGatherJs / 2, false>(abort_flag, ps, plim, src, n, tag, out)
+                                : ll_gather2_j<kGatherJ / 2, false>(abort_flag, ps, plim, src, n, tag, out);
 }
 // Word index of slot j of this thread in a pair gather (and the channel a thread owns in
 // the residual / LayerNorm passes, which follow the same order).
@@ -243,7 +243,7 @@ __device__ __forceinline__ int pair_slot(int tid, int j) { return 2 * (tid + (j 
 // The LM-head pick: pair k = (value, index bits) at words k * kPersistLmStride + {0, 1},
 // one 16-byte poll per pair, into vals[k] / idx[k] (shared memory).
 template <bool SYS>
-__device__ __noinline__ bool ll_gather_pairs(int* abort_flag, const PeerSet* ps, const unsigned long long* src,
+__device__ __noinline__ bool ll_gather_pairs(int* abort_flag, const PeerSet* ps, uint32_t plim, const unsigned long long* src,
                                              int npairs, uint32_t tag, float* vals, int* idx) {
     constexpr int J = kMaxCtas * 8 / kCT + 1;  // pairs per thread (8 ranks of kMaxCtas CTAs)
     const int tid = threadIdx.x;
@@ -269,16 +269,16 @@ __device__ __noinline__ bool ll_gather_pairs(int* abort_flag, const PeerSet* ps,
             }
         }
         if (!pending) break;
-        if (it > kPollLimit) { give_up(abort_flag, ps); return false; }
+        if (it > plim) { give_up(abort_flag, ps); return false; }
         if ((it & 15) == 15 && aborted(abort_flag)) return false;
         __nanosleep(32);
     }
     return true;
 }
 // Words written by the ranks of a tensor-parallel group (system scope, 32-word rounds).
-__device__ __forceinline__ bool ll_gather_group(int* abort_flag, const PeerSet* ps, const unsigned long long* src,
+__device__ __forceinline__ bool ll_gather_group(int* abort_flag, const PeerSet* ps, uint32_t plim, const unsigned long long* src,
                                                 int n, uint32_t tag, float* out) {
-    return ll_gather_j<kGatherJ, true>(abort_flag, ps, src, n, tag, out);
+    return ll_gather_j<kGatherJ, true>(abort_flag, ps, plim, src, n, tag, out);
 }
 
 // consumer-only barriers (named barrier 1, the 256 consumer threads)
@@ -631,6 +631,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
     }
     const int b = blockIdx.x;
     const int unit_bytes = C * kWB;  // one row-unit: a row of K = C, half a K-half of K = 4C
+    const uint32_t plim = P.poll_limit;  // polls of one exchange wait before it gives up
     const uint32_t epoch0 = *P.d_epoch;
     const int pos0 = *P.d_pos;
     int tok = *P.d_token;
@@ -774,7 +775,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                 unsigned f;
                 asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(f) : "l"(flag) : "memory");
                 if ((int)(f - need) >= 0) break;
-                if (it > kPollLimit) { give_up(P.abort_flag, pgp); bad = true; return; }
+                if (it > plim) { give_up(P.abort_flag, pgp); bad = true; return; }
                 if ((it & 15) == 15 && aborted(P.abort_flag)) { bad = true; return; }
                 __nanosleep(64);
             }
@@ -820,6 +821,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                 const int l = lm ? 0 : (u >> 2);
                 const int ph = lm ? kPhLm : (u & 3);
                 XT* xv = reinterpret_cast<XT*>(xs);
+                // 8-bit tensor-core stages take x as FP16, scaled by 2^-e so that max |x| lands in
+                // [2^14, 2^15): no overflow for large activations, full precision for small ones;
+                // the row sums are multiplied back by 2^e (exact).  xmax: this thread's max |x|.
+                float xmax = 0.0f, x_up = 1.0f;
 
                 // ---------- x of this phase ----------
                 if (ph == kPhQkv || ph == kPhFc || lm) {
@@ -869,7 +874,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                         const unsigned long long* src = ((ph == kPhFc) ? P.ll_proj : P.ll_fcproj) + lsrc * TP * C;
                         bool ok = true;
                         if constexpr (!TPG) {
-                            ok = ll_gather2<WIDE>(P.abort_flag, pgp, src, C, tag, gv);
+                            ok = ll_gather2<WIDE>(P.abort_flag, pgp, plim, src, C, tag, gv);
 #pragma unroll
                             for (int j = 0; j < kCPT; j++) {
                                 const int c = pair_slot(tid, j);
@@ -880,7 +885,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                             // order (the same on every rank), rounded as the single-GPU store
                             const int n = TP * C;
                             for (int base = 0; base < n && ok; base += kGatherJ * kCT) {
-                                ok = ll_gather_group(P.abort_flag, pgp, src + base, min(n - base, kGatherJ * kCT), tag, gv);
+                                ok = ll_gather_group(P.abort_flag, pgp, plim, src + base, min(n - base, kGatherJ * kCT), tag, gv);
 #pragma unroll
                                 for (int j = 0; j < kGatherJ; j++)
                                     if (base + tid + j * kCT < n) red[base + tid + j * kCT] = gv[j];
@@ -940,26 +945,50 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                             const float bb = WIDE ? to_f<XT>(lnp[C + c]) : lb[j];
                             const XT xvv = from_f<XT>((rstd * (res[c] - mean)) * g + bb);
                             xv[c] = xvv;
-                            if constexpr (w8) reinterpret_cast<__half*>(xh)[c] = __float2half_rn(to_f<XT>(xvv));
+                            if constexpr (MMA && w8) xmax = fmaxf(xmax, fabsf(to_f<XT>(xvv)));
                         }
                     }
                 } else {
                     // PROJ: x = atty of this rank's heads; FCPROJ: x = gelu(fc) of this rank's FC rows
                     const int n = (ph == kPhProj) ? P.proj_k : P.fcproj_k;
                     const unsigned long long* src = (ph == kPhProj) ? P.ll_atty + (size_t)l * n : P.ll_fc + (size_t)l * n;
-                    const bool ok = ll_gather2<WIDE>(P.abort_flag, pgp, src, n, tag, gv);
+                    const bool ok = ll_gather2<WIDE>(P.abort_flag, pgp, plim, src, n, tag, gv);
 #pragma unroll
                     for (int j = 0; j < (WIDE ? kGatherJ : kGatherJs); j++) {
                         const int w = pair_slot(tid, j);
                         if (w < n) {
                             const XT xvv = from_f<XT>(gv[j]);
                             xv[w] = xvv;
-                            if constexpr (w8) reinterpret_cast<__half*>(xh)[w] = __float2half_rn(to_f<XT>(xvv));
+                            if constexpr (MMA && w8) xmax = fmaxf(xmax, fabsf(to_f<XT>(xvv)));
                         }
                     }
                     if (cta_any(!ok)) goto consumer_abort;
                 }
+                if constexpr (MMA && w8) {
+                    xmax = warp_max(xmax);
+                    if (lane == 0) misc[kXmaxSlot + warp] = xmax;
+                }
                 cta_sync();
+                if constexpr (MMA && w8) {
+                    // the CTA's max |x| (NaN entries are skipped by fmaxf and stay NaN), then each
+                    // warp converts the 32-value units of x its stage products read
+                    float am = misc[kXmaxSlot];
+#pragma unroll
+                    for (int w = 1; w < kCW; w++) am = fmaxf(am, misc[kXmaxSlot + w]);
+                    int e = 0;
+                    if (am > 0.0f) e = (am <= FLT_MAX) ? ((__float_as_int(am) >> 23) & 0xff) - 127 - 14 : 100;
+                    e = max(-100, min(100, e));
+                    const float x_down = __int_as_float((127 - e) << 23);
+                    x_up = __int_as_float((127 + e) << 23);
+                    const PhaseRows& pg = geo[ph];
+                    const int nku = pg.part >> 5;
+                    for (int kq = 0; kq < pg.kparts; kq++)
+                        for (int ku = warp; ku < nku; ku += kCW) {
+                            const int i = kq * pg.part + ku * 32 + lane;
+                            reinterpret_cast<__half*>(xh)[i] = __float2half_rn(to_f<XT>(xv[i]) * x_down);
+                        }
+                    __syncwarp();
+                }
                 PTRACE(u * 3 + 0);
 
                 // ---------- the matrix rows of this CTA ----------
@@ -1141,7 +1170,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
 #pragma unroll
                                     for (int w = 0; w < kCW; w++) v += mr[w * 16 + tid];
                                     k0 += v;
-                                    if (last && tid < nr) emit(sd, r0, tid, k0);
+                                    if (last && tid < nr) emit(sd, r0, tid, w8 ? k0 * x_up : k0);
                                 }
                                 if (warp == 0) {
                                     __syncwarp();
@@ -1175,7 +1204,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                         for (uint32_t it = 0;; ++it) {
                             const unsigned long long w = ll_load(src);
                             if ((uint32_t)(w >> 32) == tag) { v = __uint_as_float((uint32_t)w); break; }
-                            if (it > kPollLimit) { give_up(P.abort_flag, pgp); bad = true; break; }
+                            if (it > plim) { give_up(P.abort_flag, pgp); bad = true; break; }
                             if ((it & 15) == 15 && aborted(P.abort_flag)) { bad = true; break; }
                             __nanosleep(32);
                         }
@@ -1341,7 +1370,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                     } else {
                         // split 0 merges the head's partials and publishes atty
                         const int nw = (s_eff - 1) * (kHSz + 2);  // <= 31 * 66 <= 8 * kCT
-                        if (!ll_gather2<WIDE>(P.abort_flag, pgp, part + (kHSz + 2), nw, tag, gv)) bad = true;
+                        if (!ll_gather2<WIDE>(P.abort_flag, pgp, plim, part + (kHSz + 2), nw, tag, gv)) bad = true;
 #pragma unroll
                         for (int j = 0; j < 8; j++)
                             if (pair_slot(tid, j) < nw) mrg[pair_slot(tid, j)] = gv[j];
@@ -1400,7 +1429,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
             {
                 float* gvals = reinterpret_cast<float*>(xs);
                 int* gidx = reinterpret_cast<int*>(xs) + NG;
-                const bool ok = ll_gather_pairs<TPG>(P.abort_flag, pgp, P.ll_lm, NG, tag, gvals, gidx);
+                const bool ok = ll_gather_pairs<TPG>(P.abort_flag, pgp, plim, P.ll_lm, NG, tag, gvals, gidx);
                 if (cta_any(!ok)) goto consumer_abort;
                 PTRACE(4 * L * 3 + 2);
                 float bv = -FLT_MAX;

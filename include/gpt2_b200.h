@@ -255,8 +255,14 @@ enum {
     GPT2B_OPT_USE_PDL = 2,    /* 1 (default): programmatic dependent launch between kernels */
     GPT2B_OPT_SPLITS = 3,     /* attention splits per head for long contexts (default: fills the SMs) */
     GPT2B_OPT_STEPS_PER_GRAPH = 4, /* decode steps captured into one graph (default 8) */
-    GPT2B_OPT_PERSISTENT = 5  /* 1 (default where the shape allows): the whole decode loop runs in one
+    GPT2B_OPT_PERSISTENT = 5, /* 1 (default where the shape allows): the whole decode loop runs in one
                                  cooperative kernel; 0: per-kernel steps (GEMV / attention launches) */
+    GPT2B_OPT_POLL_LIMIT = 6  /* persistent kernel: polls of one wait on another CTA (or another rank of a
+                                 tensor-parallel group) before it gives up, records
+                                 GPT2B_DEVERR_GRID_TIMEOUT and makes every CTA of the group leave
+                                 (default 4194304, a few seconds; at least 1024).  After a timeout in a
+                                 tensor-parallel group the exchange words of the aborted call are
+                                 stale: destroy and rebuild the group's engines. */
 };
 
 /* GPT2Config field order (Inference_gpt2/gpt2_model.h:28-35). */

@@ -86,7 +86,7 @@ _REF_CPU_SIGS = {
     "gelu": {"ref_gelu_cpu": (None, [_P, _P, _I])},
     "encoder": {"ref_encoder_cpu": (None, [_P, _P, _P, _P, _I, _I, _I])},
     "decode": {"ref_decoder_create": (_P, [_P, _P]), "ref_decoder_step": (_I, [_P, _I, _I, _P]),
-               "ref_decoder_free": (None, [_P])},
+               "ref_decoder_free": (None, [_P]), "ref_set_threads": (_I, [_I])},
 }
 
 

@@ -7,6 +7,7 @@
  * would run on one thread at batch 1.
  * TEST INFRASTRUCTURE: bench.py's reference arm and cpu_baseline leg time it. */
 #include <math.h>
+#include <omp.h>
 #include <stdlib.h>
 #include <string.h>
 #include <vector>
@@ -48,6 +49,13 @@ REFAPI void* ref_decoder_create(const int* cfg6, const float* params) {
 }
 
 REFAPI void ref_decoder_free(void* h) { delete (RefDecoder*)h; }
+
+/* OpenMP threads of the GEMV loops (a launcher may have set OMP_NUM_THREADS=1
+ * for its ranks); returns the count now in effect. */
+REFAPI int ref_set_threads(int n) {
+    if (n > 0) omp_set_num_threads(n);
+    return omp_get_max_threads();
+}
 
 static void linear(RefDecoder* d, float* out, const float* W, const float* b, const float* x, int M, int K) {
     ref_gemv_cpu_f32(out, W, x, M, K);

@@ -197,6 +197,39 @@ def test_wide_model_persistent_matches_kernel_path(gpt2b, orc, cuda, wmode, kvmo
     assert min(cos_o) >= 0.999, min(cos_o)
 
 
+@pytest.mark.slow
+@pytest.mark.parametrize("wmode", ["int8", "fp8"])
+def test_wide_model_extreme_activations(gpt2b, orc, cuda, wmode):
+    """The wide persistent kernel feeds 8-bit weights to tensor-core stages with
+    x in FP16 after a power-of-two prescale.  Layer 0's LN1 output is pushed far
+    above FP16's range (gamma x 3e5) and the final LN output far below its
+    normal range (gamma, beta x 1e-6, so the logits are proportional to those
+    tiny values): the logits must still follow the oracle and the per-kernel
+    path (FP32 CUDA-core GEMVs)."""
+    from cuda_gpt2_inference_b200 import weights
+    cfg = weights.mini_config(L=2, NH=20, maxT=128, V=500, Vp=512)
+    p = weights.synth_params(cfg, 9, init="test")
+    p["ln1w"][0] *= np.float32(3e5)
+    p["lnfw"] *= np.float32(1e-6)
+    p["lnfb"] *= np.float32(1e-6)
+    img, sc = _quantize(gpt2b, weights.image(p, cfg, "bf16"), wmode)
+    prompt = [9, 8, 7]
+    ek = _engine(img, wmode, "floatx", sc, "kernels")
+    toks, lk = ek.generate(prompt, 40, want_logits=True)
+    ek.close()
+    seq = list(prompt) + list(toks[:-1])
+    ep = _engine(img, wmode, "floatx", sc, "persistent")
+    _, lp = ep.generate(seq, 0, want_logits=True)
+    ep.close()
+    assert np.isfinite(lp).all()
+    assert float(np.abs(lp).max()) < 1e-3  # the logits really are tiny
+    cos = [cosine(lk[i], lp[i]) for i in range(len(seq))]
+    assert min(cos) >= 0.999, (min(cos), int(np.argmin(cos)))
+    m = orc.Model(img, wmode, "floatx", sc)
+    cos_o = [cosine(lp[i], m.step(int(t), i)) for i, t in enumerate(seq)]
+    assert min(cos_o) >= 0.999, min(cos_o)
+
+
 def test_engine_rejects_bad_inputs(mini, gpt2b):
     cfg, imgs = mini
     eng = _engine(imgs["bf16"][0], "bf16")
