@@ -255,30 +255,30 @@ def flat_params_124m(params):
     return np.ascontiguousarray(flat, np.float32)
 
 
-def flat_params_from_w8(img, sc, cfg):
-    """The 16 tensors of an 8-bit mixed image as FP32: the five Linear groups
-    dequantised (code x row scale), the rest widened from BF16."""
+def flat_params_cpu(cfg, fmt=None, seed=1234):
+    """The 16 tensors of the benchmark model as FP32, built on the host only:
+    BF16-rounded, and for ``fmt`` in {"int8", "fp8"} the five Linear groups
+    quantised per row (the checker's restatement of quantize.cu) and
+    dequantised (code x row scale) -- the weights the reference's CPU loops
+    multiply."""
+    import oracle
     from cuda_gpt2_inference_b200 import weights
     shp = weights.shapes(cfg)
-    total = sum(int(np.prod(v)) for v in shp.values())
-    flat = np.empty(total, np.float32)
-    buf = np.frombuffer(img, np.uint8)
-    off, foff, soff = 1024, 0, 0
-    for name in weights.NAMES:
-        n = int(np.prod(shp[name]))
-        if name in weights.LINEAR:
-            rows = n // cfg["C"] if name != "fcprojw" else n // (4 * cfg["C"])
-            codes = buf[off:off + n].view(np.int8).reshape(rows, -1)
-            s = sc[soff:soff + rows]
-            for r0 in range(0, rows, 8192):  # chunks keep the temporaries small
-                flat[foff + r0 * codes.shape[1]: foff + (r0 + codes[r0:r0 + 8192].shape[0]) * codes.shape[1]] = \
-                    (codes[r0:r0 + 8192].astype(np.float32) * s[r0:r0 + 8192, None]).ravel()
-            off += n
-            soff += rows
+    flat = np.empty(sum(int(np.prod(v)) for v in shp.values()), np.float32)
+    foff = 0
+    for name, a in weights.param_stream(cfg, seed, "spec"):
+        a = weights.bf16_to_f32(weights.bf16_bits(a)).reshape(-1, a.shape[-1])
+        n = a.size
+        if fmt and name in weights.LINEAR:
+            for r0 in range(0, a.shape[0], 8192):  # row blocks keep the temporaries small
+                blk = a[r0:r0 + 8192]
+                q, sc = oracle.quant_rows(blk, fmt)
+                flat[foff + r0 * a.shape[1]: foff + r0 * a.shape[1] + blk.size] = \
+                    oracle.dequant_rows(q, sc, fmt).ravel()
         else:
-            flat[foff:foff + n] = weights.bf16_to_f32(buf[off:off + 2 * n].view(np.uint16))
-            off += 2 * n
+            flat[foff:foff + n] = a.ravel()
         foff += n
+        del a
     return flat
 
 
@@ -308,7 +308,7 @@ class CpuDecoder:
 
 
 def cpu_baseline_124m(params, cfg, budget_s=15.0):
-    dec = CpuDecoder(flat_params_124m(params), cfg)
+    dec = CpuDecoder(flat_params_124m(params), cfg)  # FP32 math; only the time is used
     dec.time_positions([PROMPT_LEN])  # warm-up
     probe = dec.time_positions(spread_positions(2))
     n = int(max(4, min(64, budget_s * 1e3 / max(probe, 1e-3))))
@@ -329,22 +329,20 @@ def run_reference(args, rank, world):
         print(json.dumps({"impl": "reference", "unavailable": "reference CPU loops were not built (oracle/_ref)"}))
         return 0
     if args.config == XL_CONFIG:
-        cfg, img, sc = xl_model(0, 1)
-        flat = flat_params_from_w8(img, sc, cfg)
-        del img
+        cfg = weights.GPT2_XL
+        flat = flat_params_cpu(cfg, "int8")
         metric, dtype = XL_METRIC, "f32"
         wl = "gpt2-xl greedy decode (int8 weights dequantised to FP32), CPU reference loops"
         what = "FP32 math on the dequantised INT8 weights"
         par = f"reference CPU path (tp{world} on the GPU arm)"
     else:
         cfg = weights.GPT2_124M
-        wmode, kvmode = CONFIGS.get(args.config, ("bf16", "floatx"))
+        wmode, kvmode = CONFIGS.get(args.config, ("fp8", "8bit") if args.config == LONG_CONFIG else ("bf16", "floatx"))
         if wmode in ("int8", "fp8"):
-            _, _, img, sc = make_model(wmode, kvmode)
-            flat = flat_params_from_w8(img, sc, cfg)
+            flat = flat_params_cpu(cfg, wmode)
             what = f"FP32 math on the dequantised {wmode.upper()} weights"
         else:
-            flat = flat_params_124m(weights.synth_params(cfg, 1234, init="spec"))
+            flat = flat_params_cpu(cfg)
             what = "FP32 math on the BF16 weights"
         metric, dtype = METRIC, "f32"
         wl = "gpt2-124m greedy decode, CPU reference loops"

@@ -34,7 +34,8 @@ ERR_CUDA = 2000
 # weight / KV modes
 W_F32, W_BF16, W_INT8, W_FP8 = 0, 1, 2, 3
 KV_FLOATX, KV_8BIT = 0, 1
-OPT_USE_GRAPH, OPT_USE_PDL, OPT_SPLITS, OPT_STEPS_PER_GRAPH, OPT_PERSISTENT, OPT_POLL_LIMIT = 1, 2, 3, 4, 5, 6
+OPT_USE_GRAPH, OPT_USE_PDL, OPT_SPLITS, OPT_STEPS_PER_GRAPH, OPT_PERSISTENT, OPT_POLL_LIMIT, OPT_PREFILL = \
+    1, 2, 3, 4, 5, 6, 7
 # device error codes (gpt2b_device_error)
 DEVERR_GRID_TIMEOUT = 5
 
@@ -80,6 +81,10 @@ _SIGS = {
     "gpt2b_attention_kv_split_bf16": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
     "gpt2b_attention_kv_merge_bf16": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "gpt2b_attention_kv_merge_f32": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P]),
+    "gpt2b_attention_kv_split_f32": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
+    "gpt2b_attention_kv_split_w8_i8": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
+    "gpt2b_attention_kv_split_w8_fp8": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
+    "gpt2b_attention_kv_merge_w8": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "gpt2b_attention_forward_kv_large_bf16_noalloc": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _I, _P]),
     "gpt2b_layernorm_forward_f32": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _P]),
     "gpt2b_layernorm_forward_bf16": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _P]),
@@ -89,6 +94,14 @@ _SIGS = {
     "gpt2b_encoder_forward_kv_bf16": (_I, [_P, _P, _P, _P, _P, _I, _I, _P]),
     "gpt2b_gpu_sample_softmax": (_I, [_P, _P, _I, _I, _U64, _I, _P]),
     "gpt2b_gpu_argmax": (_I, [_P, _P, _I, _I, _I, _P]),
+    "gpt2b_logits_nll": (_I, [_P, _P, _I, _P, _P]),
+    "gpt2b_engine_generate_dump": (_I, [_P, _P, _I, _I, _P, _I, _U64, _P, _P]),
+    "gpt2b_matmul_forward_bf16": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P]),
+    "gpt2b_matmul_forward_f32out_bf16": (_I, [_P, _P, _P, _I, _I, _I, _I, _P]),
+    "gpt2b_matmul_forward_w8_i8": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P]),
+    "gpt2b_matmul_forward_w8_fp8": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P]),
+    "gpt2b_matmul_forward_w8_i8_f32out": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P]),
+    "gpt2b_matmul_forward_w8_fp8_f32out": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "gpt2b_read_header": (_I, [_S, _P, _P]),
     "gpt2b_engine_create_from_file": (_I, [_S, _S, _I, _I, _P]),
     "gpt2b_engine_create_from_buffer": (_I, [_P, _SZ, _P, _SZ, _I, _I, _P]),

@@ -596,6 +596,31 @@ int gpt2b_attention_kv_split_bf16(float* part_out, float* part_lse, float* part_
     return attn_split(KV_BF16, part_out, part_lse, part_max, qkv, kv_cache, nullptr, B, NH, hs, maxT, S, d_pos,
                       (cudaStream_t)stream);
 }
+int gpt2b_attention_kv_split_f32(float* part_out, float* part_lse, float* part_max, const float* qkv,
+                                 const float* kv_cache, int B, int NH, int hs, int maxT, int S, const int* d_pos,
+                                 gpt2b_stream_t stream) {
+    return attn_split(KV_F32, part_out, part_lse, part_max, qkv, kv_cache, nullptr, B, NH, hs, maxT, S, d_pos,
+                      (cudaStream_t)stream);
+}
+int gpt2b_attention_kv_split_w8_i8(float* part_out, float* part_lse, float* part_max, const uint16_t* qkv,
+                                   const uint8_t* kv_cache, const float* kv_scale, int B, int NH, int hs, int maxT,
+                                   int S, const int* d_pos, gpt2b_stream_t stream) {
+    if (!kv_scale) return GPT2B_ERR_INVALID_ARG;
+    return attn_split(KV_I8, part_out, part_lse, part_max, qkv, kv_cache, kv_scale, B, NH, hs, maxT, S, d_pos,
+                      (cudaStream_t)stream);
+}
+int gpt2b_attention_kv_split_w8_fp8(float* part_out, float* part_lse, float* part_max, const uint16_t* qkv,
+                                    const uint8_t* kv_cache, const float* kv_scale, int B, int NH, int hs, int maxT,
+                                    int S, const int* d_pos, gpt2b_stream_t stream) {
+    if (!kv_scale) return GPT2B_ERR_INVALID_ARG;
+    return attn_split(KV_FP8, part_out, part_lse, part_max, qkv, kv_cache, kv_scale, B, NH, hs, maxT, S, d_pos,
+                      (cudaStream_t)stream);
+}
+int gpt2b_attention_kv_merge_w8(uint16_t* out, const float* part_out, const float* part_lse, const float* part_max,
+                                int B, int NH, int hs, int S, gpt2b_stream_t stream) {
+    return attn_merge<__nv_bfloat16>((__nv_bfloat16*)out, part_out, part_lse, part_max, B, NH, hs, S,
+                                     (cudaStream_t)stream);
+}
 int gpt2b_attention_kv_merge_bf16(uint16_t* out, const float* part_out, const float* part_lse, const float* part_max,
                                   int B, int NH, int hs, int S, gpt2b_stream_t stream) {
     return attn_merge<__nv_bfloat16>((__nv_bfloat16*)out, part_out, part_lse, part_max, B, NH, hs, S,

@@ -34,6 +34,7 @@
 #include <math.h>
 #include <stdio.h>
 #include <string.h>
+#include <sys/stat.h>
 
 #include <algorithm>
 #include <string>
@@ -90,6 +91,10 @@ struct gpt2b_engine {
     float* lm_pairs = nullptr;     // every rank's pair
     float* logits_full = nullptr;  // all-gathered logits (Vp) for host copies and sampling
     bool tp_connected = false;     // peers' exchange arenas mapped (persistent kernel usable)
+    // prompt prefill on the tensor cores (prefill.cu): set up at the first prompt
+    bool prefill_ok = false, use_prefill = false, prefill_ready = false;
+    unsigned char* pf_mem = nullptr;  // activation rows [maxT] x (C | C | 3C | C | C | 4C), then maxT x Vp logits
+    PrefillPlan pf;
     unsigned char* peer_map[8] = {};  // IPC mappings of the other ranks' arenas
 #if GPT2B_HAVE_NCCL
     ncclComm_t comm = nullptr;
@@ -257,6 +262,7 @@ void free_engine(gpt2b_engine* e) {
     if (e->acts) cudaFree(e->acts);
     if (e->kv) cudaFree(e->kv);
     if (e->xchg) cudaFree(e->xchg);
+    if (e->pf_mem) cudaFree(e->pf_mem);
     if (e->stream) cudaStreamDestroy(e->stream);
     delete e;
 }
@@ -353,6 +359,63 @@ cudaError_t ensure_graphs(gpt2b_engine* e) {
     if (err == cudaSuccess && e->steps_per_graph > 1) err = capture(e, e->steps_per_graph, &e->graph_multi);
     if (err == cudaSuccess) e->graphs_valid = true;
     return err;
+}
+
+// The prefill plan: activation rows for maxT prompt tokens, the logits of
+// every prompt row, and the tensor maps of every GEMM operand (weights of
+// every layer, activations over maxT rows), built once at the first prompt.
+cudaError_t ensure_prefill(gpt2b_engine* e) {
+    if (e->prefill_ready) return cudaSuccess;
+    const gpt2b_config& c = e->cfg;
+    const size_t C = c.channels, L = c.num_layers, maxT = c.max_seq_len, Vp = c.padded_vocab_size;
+    const size_t wb = (size_t)wkind_bytes(e->wk), xb = e->xbytes;
+    const size_t widths[6] = {C, C, 3 * C, C, C, 4 * C};  // res, x, qkv, atty, proj, f
+    size_t off[7], total = 0;
+    for (int i = 0; i < 6; i++) { off[i] = total; total += align256(maxT * widths[i] * 2); }
+    off[6] = total;
+    total += align256(maxT * Vp * 4);
+    cudaError_t err = cudaMalloc(&e->pf_mem, total);
+    if (err != cudaSuccess) return err;
+    if ((err = cudaMemset(e->pf_mem, 0, total)) != cudaSuccess) return err;
+    PrefillPlan& P = e->pf;
+    P.wk = e->wk; P.kvk = e->kvk; P.C = (int)C; P.NH = c.num_heads; P.L = (int)L; P.V = c.vocab_size;
+    P.Vp = (int)Vp; P.maxT = (int)maxT;
+    P.attn_scale = 1.0f / sqrtf((float)(C / c.num_heads));
+    P.res = e->pf_mem + off[0]; P.x = e->pf_mem + off[1]; P.qkv = e->pf_mem + off[2];
+    P.atty = e->pf_mem + off[3]; P.proj = e->pf_mem + off[4]; P.f = e->pf_mem + off[5];
+    P.logits_rows = reinterpret_cast<float*>(e->pf_mem + off[6]);
+    P.tokens = e->d_prompt;
+    P.wte = e->p[0]; P.wte_scale = e->w8 ? e->sc[0] : nullptr; P.wpe = e->p[1];
+    P.lnfw = e->p[14]; P.lnfb = e->p[15];
+    P.logits_last = e->logits; P.d_token = e->d_token; P.d_pos = e->d_pos; P.history = e->d_history;
+    const int iC = (int)C, iM = (int)maxT;
+    bool ok = tc_maps(&P.a_x, nullptr, e->wk, P.x, iM, nullptr, 0, iC, false) &&
+              tc_maps(&P.a_atty, nullptr, e->wk, P.atty, iM, nullptr, 0, iC, false) &&
+              tc_maps(&P.a_f, nullptr, e->wk, P.f, iM, nullptr, 0, 4 * iC, false) &&
+              tc_maps(nullptr, &P.w_lm, e->wk, nullptr, 0, e->p[0], (int)Vp, iC, true);
+    P.s_lm = e->w8 ? e->sc[0] : nullptr;
+    P.layers.assign(L, PrefillLayer());
+    const size_t kvb = (e->kvk >= KV_I8) ? 1 : xb;
+    for (size_t l = 0; l < L && ok; l++) {
+        PrefillLayer& Y = P.layers[l];
+        ok = tc_maps(nullptr, &Y.w_qkv, e->wk, nullptr, 0, e->p[4] + l * 3 * C * C * wb, 3 * iC, iC, false) &&
+             tc_maps(nullptr, &Y.w_proj, e->wk, nullptr, 0, e->p[6] + l * C * C * wb, iC, iC, false) &&
+             tc_maps(nullptr, &Y.w_fc, e->wk, nullptr, 0, e->p[10] + l * 4 * C * C * wb, 4 * iC, iC, false) &&
+             tc_maps(nullptr, &Y.w_fcproj, e->wk, nullptr, 0, e->p[12] + l * 4 * C * C * wb, iC, 4 * iC, false);
+        Y.qkvb = e->p[5] + l * 3 * C * xb; Y.projb = e->p[7] + l * C * xb;
+        Y.fcb = e->p[11] + l * 4 * C * xb; Y.fcprojb = e->p[13] + l * C * xb;
+        if (e->w8) {
+            Y.s_qkv = e->sc[1] + l * 3 * C; Y.s_proj = e->sc[2] + l * C;
+            Y.s_fc = e->sc[3] + l * 4 * C; Y.s_fcproj = e->sc[4] + l * C;
+        }
+        Y.ln1w = e->p[2] + l * C * xb; Y.ln1b = e->p[3] + l * C * xb;
+        Y.ln2w = e->p[8] + l * C * xb; Y.ln2b = e->p[9] + l * C * xb;
+        Y.kv = e->kv_cache + l * e->kv_layer_elems * kvb;
+        Y.kv_scale = e->kv_scale ? e->kv_scale + l * e->kv_layer_scales : nullptr;
+    }
+    if (!ok) return cudaErrorNotSupported;
+    e->prefill_ready = true;
+    return cudaSuccess;
 }
 
 // n forwards from the device-resident token/position.
@@ -738,6 +801,8 @@ int build_engine(const unsigned char* image, size_t nbytes, const float* scales,
     if (lm.grid > lm_grid_max) return fail(cudaErrorInvalidConfiguration);
     e->lm_p = lm;
     if ((err = setup_persistent(e, nsm)) != cudaSuccess) return fail(err);
+    e->prefill_ok = e->use_prefill =
+        !tp && prefill_supported(e->wk, e->kvk, C, cfg.num_heads, cfg.max_seq_len);
     *out = e;
     return GPT2B_OK;
 }
@@ -953,6 +1018,10 @@ int gpt2b_engine_set_option(gpt2b_engine* e, int option, int value) {
             if (value && !e->persist_ok) return GPT2B_ERR_UNSUPPORTED;  // (tensor parallel: connect first)
             e->use_persistent = value != 0;
             break;
+        case GPT2B_OPT_PREFILL:
+            if (value && !e->prefill_ok) return GPT2B_ERR_UNSUPPORTED;
+            e->use_prefill = value != 0;
+            break;
         case GPT2B_OPT_POLL_LIMIT:
             if (value < 1024) return GPT2B_ERR_INVALID_ARG;
             e->pp.poll_limit = (uint32_t)value;
@@ -1040,11 +1109,25 @@ int gpt2b_engine_generate(gpt2b_engine* e, const int* prompt, int n_prompt, int 
     if (err == cudaSuccess) err = cudaMemcpyAsync(e->d_pos, &zero, sizeof(int), cudaMemcpyHostToDevice, st);
     if (err == cudaSuccess) err = cudaMemcpyAsync(e->d_history, prompt, sizeof(int), cudaMemcpyHostToDevice, st);
     const int total = n_prompt + n_gen;
+    int first = 0;  // forwards already done
+    if (err == cudaSuccess && e->use_prefill && n_prompt >= 2) {
+        // the whole prompt as tensor-core GEMMs: positions 0..n_prompt-1 in one pass
+        err = ensure_prefill(e);
+        if (err == cudaSuccess) err = run_prefill(e->pf, n_prompt, st);
+        if (err == cudaSuccess && logits_host)
+            err = cudaMemcpyAsync(logits_host, e->pf.logits_rows, (size_t)n_prompt * Vp * 4, cudaMemcpyDeviceToHost, st);
+        if (err == cudaSuccess && sample) {  // the token after the prompt is drawn, not picked
+            int rc = gpt2b_gpu_sample_softmax(e->d_token, e->logits, 1, V, seed, n_prompt, (gpt2b_stream_t)st);
+            if (rc) return rc;
+            err = launch_k(set_history_kernel, dim3(1), dim3(1), 0, st, false, e->d_history, e->d_token, e->d_pos);
+        }
+        first = n_prompt;
+    }
     if (err == cudaSuccess) {
         if (!logits_host && !sample) {
-            err = run_steps(e, total);  // device-resident: no host round trip per token
+            err = run_steps(e, total - first);  // device-resident: no host round trip per token
         } else {
-            for (int s = 0; s < total && err == cudaSuccess; s++) {
+            for (int s = first; s < total && err == cudaSuccess; s++) {
                 err = run_steps(e, 1);
                 float* lg = e->logits;  // all Vp logits (tensor parallel: gathered from the vocab shards)
                 if (err == cudaSuccess && e->tp_size > 1) {
@@ -1074,3 +1157,133 @@ int gpt2b_engine_generate(gpt2b_engine* e, const int* prompt, int n_prompt, int 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// verification dumps (Inference_gpt2/dump_utils.h)
+// ---------------------------------------------------------------------------
+namespace {
+
+bool mkdir_p(const std::string& dir) {
+    std::string cur;
+    for (size_t i = 0; i < dir.size(); i++) {
+        cur += dir[i];
+        if ((dir[i] == '/' && i > 0) || i + 1 == dir.size()) {
+            if (mkdir(cur.c_str(), 0755) != 0) {
+                struct stat st;
+                if (stat(cur.c_str(), &st) != 0 || !S_ISDIR(st.st_mode)) return false;
+            }
+        }
+    }
+    return true;
+}
+
+bool write_file(const std::string& path, const void* data, size_t bytes) {
+    FILE* f = fopen(path.c_str(), "wb");
+    if (!f) return false;
+    const bool ok = fwrite(data, 1, bytes, f) == bytes;
+    return fclose(f) == 0 && ok;
+}
+
+}  // namespace
+
+extern "C" int gpt2b_engine_generate_dump(gpt2b_engine* e, const int* prompt, int n_prompt, int n_gen,
+                                          int* out_tokens, int sample, unsigned long long seed,
+                                          const gpt2b_dump_config* dump, float* nll_out) {
+    if (!e || !prompt || !out_tokens || !dump || n_prompt < 1 || n_gen < 0) return GPT2B_ERR_INVALID_ARG;
+    const int maxT = e->cfg.max_seq_len, V = e->cfg.vocab_size;
+    const int total = n_prompt + n_gen;
+    if (total > maxT || dump->ppl_len < 0 || dump->ppl_len > total || dump->n_steps < 0 ||
+        (dump->n_steps && !dump->steps))
+        return GPT2B_ERR_INVALID_ARG;
+    for (int i = 0; i < n_prompt; i++)
+        if (prompt[i] < 0 || prompt[i] >= V) return GPT2B_ERR_INVALID_ARG;
+    std::string dir, prefix = dump->prefix ? dump->prefix : "gpt2b";
+    if (dump->dir) {
+        dir = dump->dir;
+        if (!mkdir_p(dir)) return GPT2B_ERR_FILE;
+        if (dir.back() != '/') dir += '/';
+    }
+    DeviceGuard g(e->device);
+    cudaStream_t st = e->stream;
+    float* d_nll = nullptr;
+    cudaError_t err = cudaSuccess;
+    if (dump->ppl_len > 0) err = cudaMalloc(&d_nll, (size_t)dump->ppl_len * sizeof(float));
+    set_prompt_len(e, n_prompt);
+    const int zero = 0;
+    if (err == cudaSuccess)
+        err = cudaMemcpyAsync(e->d_prompt, prompt, (size_t)n_prompt * sizeof(int), cudaMemcpyHostToDevice, st);
+    if (err == cudaSuccess) err = cudaMemcpyAsync(e->d_token, prompt, sizeof(int), cudaMemcpyHostToDevice, st);
+    if (err == cudaSuccess) err = cudaMemcpyAsync(e->d_pos, &zero, sizeof(int), cudaMemcpyHostToDevice, st);
+    if (err == cudaSuccess) err = cudaMemcpyAsync(e->d_history, prompt, sizeof(int), cudaMemcpyHostToDevice, st);
+    std::vector<float> lg(V);
+    std::vector<int> hist;
+    int rc = GPT2B_OK;
+    // the prompt as in gpt2b_engine_generate: one tensor-core pass when prefill is on, and
+    // step t <= n_prompt then reads row t - 1 of the prompt logits
+    const bool pf = e->use_prefill && n_prompt >= 2;
+    if (pf && err == cudaSuccess) {
+        err = ensure_prefill(e);
+        if (err == cudaSuccess) err = run_prefill(e->pf, n_prompt, st);
+    }
+    for (int t = 1; t <= total && err == cudaSuccess && rc == GPT2B_OK; t++) {
+        const bool in_prompt = pf && t <= n_prompt;
+        const float* logits = in_prompt ? e->pf.logits_rows + (size_t)(t - 1) * e->cfg.padded_vocab_size : e->logits;
+        if (!in_prompt) err = run_steps(e, 1);  // the forward at position t - 1
+        if (err == cudaSuccess && !in_prompt && e->tp_size > 1) {
+            err = tp_allgather(e, e->logits, e->logits_full, (size_t)e->v_rows);
+            logits = e->logits_full;
+        }
+        if (err == cudaSuccess && sample && t >= n_prompt) {
+            rc = gpt2b_gpu_sample_softmax(e->d_token, logits, 1, V, seed, t, (gpt2b_stream_t)st);
+            if (rc == GPT2B_OK)
+                err = launch_k(set_history_kernel, dim3(1), dim3(1), 0, st, false, e->d_history, e->d_token, e->d_pos);
+        }
+        if (err == cudaSuccess && rc == GPT2B_OK && t <= dump->ppl_len)
+            err = in_prompt ? launch_nll(d_nll, logits, V, nullptr, e->d_history, nullptr, t, st)
+                            : launch_nll(d_nll, logits, V, nullptr, e->d_history, e->d_pos, 0, st);
+        const bool want_step = std::find(dump->steps, dump->steps + dump->n_steps, t) != dump->steps + dump->n_steps;
+        if (err == cudaSuccess && rc == GPT2B_OK && !dir.empty() && ((dump->logits_t1 && t == 1) || want_step)) {
+            err = cudaMemcpyAsync(lg.data(), logits, (size_t)V * sizeof(float), cudaMemcpyDeviceToHost, st);
+            hist.resize(t);
+            if (err == cudaSuccess)
+                err = cudaMemcpyAsync(hist.data(), e->d_history, (size_t)t * sizeof(int), cudaMemcpyDeviceToHost, st);
+            if (err == cudaSuccess) err = cudaStreamSynchronize(st);
+            if (err == cudaSuccess && dump->logits_t1 && t == 1 &&
+                !write_file(dir + prefix + "_logits_t1.bin", lg.data(), lg.size() * sizeof(float)))
+                rc = GPT2B_ERR_FILE;
+            if (err == cudaSuccess && want_step) {
+                const std::string ts = std::to_string(t);
+                if (!write_file(dir + prefix + "_logits_step" + ts + ".bin", lg.data(), lg.size() * sizeof(float)) ||
+                    !write_file(dir + prefix + "_inputs_step" + ts + ".bin", hist.data(), hist.size() * sizeof(int)))
+                    rc = GPT2B_ERR_FILE;
+            }
+        }
+    }
+    std::vector<float> nll(dump->ppl_len);
+    std::vector<int> ptoks(dump->ppl_len);
+    if (err == cudaSuccess && rc == GPT2B_OK) {
+        err = cudaMemcpyAsync(out_tokens, e->d_history + n_prompt, (size_t)(n_gen + 1) * sizeof(int),
+                              cudaMemcpyDeviceToHost, st);
+        if (err == cudaSuccess && dump->ppl_len > 0) {
+            err = cudaMemcpyAsync(nll.data(), d_nll, nll.size() * sizeof(float), cudaMemcpyDeviceToHost, st);
+            if (err == cudaSuccess)
+                err = cudaMemcpyAsync(ptoks.data(), e->d_history + 1, ptoks.size() * sizeof(int),
+                                      cudaMemcpyDeviceToHost, st);
+        }
+        if (err == cudaSuccess) err = cudaStreamSynchronize(st);
+    }
+    if (d_nll) cudaFree(d_nll);
+    if (err != cudaSuccess) return status_from(err);
+    if (rc != GPT2B_OK) return rc;
+    int dev = 0;
+    gpt2b_device_error(&dev);
+    if (dev) return GPT2B_ERR_DEVICE;
+    if (dump->ppl_len > 0) {
+        if (nll_out) memcpy(nll_out, nll.data(), nll.size() * sizeof(float));
+        if (!dir.empty() &&
+            (!write_file(dir + "ppl_" + prefix + "_nll.bin", nll.data(), nll.size() * sizeof(float)) ||
+             !write_file(dir + "ppl_" + prefix + "_tokens.bin", ptoks.data(), ptoks.size() * sizeof(int))))
+            return GPT2B_ERR_FILE;
+    }
+    return GPT2B_OK;
+}

@@ -1,8 +1,11 @@
 // internal.h -- interfaces between the library's translation units.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <vector>
 
 namespace gpt2b {
 
@@ -93,6 +96,11 @@ cudaError_t launch_attention_engine(int kv, const void* qkv, void* kv_layer, flo
                                     cudaStream_t st, bool pdl);
 int attn_engine_max_chunk(int kv);  // positions one engine CTA stages at once
 
+// Negative log-likelihood of a token under softmax(logits[0..V)) (sampler.cu):
+// token *tok -> out[0], or hist[p] -> out[p - 1] with p = *pos (pos non-null) or fixed_pos.
+cudaError_t launch_nll(float* out, const float* logits, int V, const int* tok, const int* hist, const int* pos,
+                       int fixed_pos, cudaStream_t st);
+
 // Persistent decode kernel (persistent.cu): every step of a decode call in
 // one cooperative launch of G CTAs (one per SM).
 struct PersistParams {
@@ -161,5 +169,57 @@ bool plan_gemv(GemvParams& p, int wk, int nsm, bool single_wave);
 size_t gemv_smem_bytes(const GemvParams& p, int wk);
 // Dispatches to the kernel instance for (wk, output float?, prologue, epilogue).
 cudaError_t launch_gemv(const GemvParams& p, int wk, bool out_f32, int pro, int epi, cudaStream_t s, bool pdl);
+
+// ---------------------------------------------------------------------------
+// Prompt prefill on the tensor cores (prefill.cu)
+// ---------------------------------------------------------------------------
+// One tcgen05 GEMM launch: out[T x N] = epilogue(A[T x K] . W[N x K]^T).
+struct TcGemmArgs {
+    int T = 0, N = 0, K = 0;      // token rows, output columns, reduction
+    const void* bias = nullptr;   // N, BF16 (may be null)
+    const float* scale = nullptr; // N per-row scales of 8-bit weights
+    void* out = nullptr;          // T x ldo: BF16, or FP32 for the LM-head form
+    void* pre_gelu = nullptr;     // T x ldo BF16 pre-activation (may be null)
+    int ldo = 0;
+    int do_gelu = 0;
+};
+// Tensor maps of one GEMM (A: BF16 activations [act_rows x K], B: weights
+// [N x K] BF16 or 8-bit codes); either pointer may be null to skip its map.
+bool tc_maps(CUtensorMap* a, CUtensorMap* b, int wk, const void* act, int act_rows, const void* W, int N, int K,
+             bool out_f32);
+cudaError_t launch_tc_gemm(int wk, const CUtensorMap& a, const CUtensorMap& b, const TcGemmArgs& g, bool out_f32,
+                           cudaStream_t st);
+
+struct PrefillLayer {
+    CUtensorMap w_qkv, w_proj, w_fc, w_fcproj;  // weight maps of this layer
+    const void *qkvb = nullptr, *projb = nullptr, *fcb = nullptr, *fcprojb = nullptr;
+    const float *s_qkv = nullptr, *s_proj = nullptr, *s_fc = nullptr, *s_fcproj = nullptr;  // 8-bit row scales
+    const void *ln1w = nullptr, *ln1b = nullptr, *ln2w = nullptr, *ln2b = nullptr;
+    unsigned char* kv = nullptr;  // this layer's [K|V][head][maxT][64] cache
+    float* kv_scale = nullptr;    // and its 8-bit row scales [K|V][head][maxT]
+};
+struct PrefillPlan {
+    int wk = 0, kvk = 0, C = 0, NH = 0, L = 0, V = 0, Vp = 0, maxT = 0;
+    float attn_scale = 0.125f;
+    // activation maps over maxT rows: x (LayerNorm outputs), atty, f (GELU outputs)
+    CUtensorMap a_x, a_atty, a_f, w_lm;
+    const float* s_lm = nullptr;
+    void *res = nullptr, *x = nullptr, *qkv = nullptr, *atty = nullptr, *proj = nullptr, *f = nullptr;  // BF16 rows
+    float* logits_rows = nullptr;  // maxT x Vp
+    const int* tokens = nullptr;   // device prompt
+    const void* wte = nullptr;     // BF16 rows or 8-bit codes
+    const float* wte_scale = nullptr;
+    const void* wpe = nullptr;
+    const void *lnfw = nullptr, *lnfb = nullptr;
+    float* logits_last = nullptr;  // the engine's logits (Vp) receive row T-1
+    int *d_token = nullptr, *d_pos = nullptr, *history = nullptr;
+    std::vector<PrefillLayer> layers;
+};
+bool prefill_supported(int wk, int kvk, int C, int NH, int maxT);
+// The whole prompt (positions 0..T-1) in one pass: KV cache filled, logits of
+// every prompt row in logits_rows, the engine's token/position/history
+// advanced to position T with the greedy pick of row T-1.
+cudaError_t run_prefill(const PrefillPlan& P, int T, cudaStream_t st);
+int prefill_device_error();
 
 }  // namespace gpt2b

@@ -808,8 +808,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
     {
         const XT* wpe = reinterpret_cast<const XT*>(P.wpe);
         float gv[(WIDE || TPG) ? kGatherJ : kGatherJs];
-        float ln_shift = 0.0f;  // the last LayerNorm's mean (the same in every consumer thread)
         for (int step = 0; step < P.n_steps; step++) {
+            // the last LayerNorm's mean within this step (the same in every consumer thread);
+            // zero at each step's first LayerNorm, so a step's arithmetic does not depend on
+            // how the steps are split into calls
+            float ln_shift = 0.0f;
             const uint32_t tag = epoch0 + (uint32_t)step + 1u;
             const int pos = pos0 + step;
             PTRACE(kTraceEv - 1);

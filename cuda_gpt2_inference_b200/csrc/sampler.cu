@@ -116,6 +116,51 @@ __global__ void __launch_bounds__(kArgThreads) argmax_kernel(int* out_token, con
     }
 }
 
+constexpr int kNllThreads = 1024;
+
+// Negative log-likelihood of one token under softmax(logits[0..V)): the
+// reference's ppl_record_nll (Inference_gpt2/dump_utils.h:63-79) on the
+// device, with no logits copy to the host.  The maximum, the sum of
+// exp(l - max) accumulated in double, nll = max + log(sum) - l[token].
+// The token is *tok (hist null; result in out[0]) or hist[p], the token the
+// engine appended at position p (result in out[p - 1]), with p = *pos, or
+// fixed_pos when pos is null.
+__global__ void __launch_bounds__(kNllThreads)
+    nll_kernel(float* out, const float* logits, int V, const int* tok, const int* hist, const int* pos, int fixed_pos) {
+    __shared__ float smx[32];
+    __shared__ double ssum[32];
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    float mx = -FLT_MAX;
+    for (int i = tid; i < V; i += kNllThreads) mx = fmaxf(mx, logits[i]);
+    mx = warp_max(mx);
+    if (lane == 0) smx[w] = mx;
+    __syncthreads();
+    mx = smx[0];
+    for (int k = 1; k < kNllThreads / 32; k++) mx = fmaxf(mx, smx[k]);
+    double s = 0.0;
+    for (int i = tid; i < V; i += kNllThreads) s += exp((double)logits[i] - (double)mx);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) ssum[w] = s;
+    __syncthreads();
+    if (tid == 0) {
+        double total = 0.0;
+        for (int k = 0; k < kNllThreads / 32; k++) total += ssum[k];
+        const int p = pos ? *pos : fixed_pos;
+        const int t = hist ? hist[p] : *tok;
+        if (t < 0 || t >= V || (hist && p < 1)) {
+            report_device_error(GPT2B_DEVERR_BAD_TOKEN);
+            return;
+        }
+        out[hist ? p - 1 : 0] = (float)((double)mx + log(total) - (double)logits[t]);
+    }
+}
+
+cudaError_t launch_nll(float* out, const float* logits, int V, const int* tok, const int* hist, const int* pos,
+                       int fixed_pos, cudaStream_t st) {
+    return launch_k(nll_kernel, dim3(1), dim3(kNllThreads), 0, st, false, out, logits, V, tok, hist, pos, fixed_pos);
+}
+
 }  // namespace gpt2b
 
 using namespace gpt2b;
@@ -126,6 +171,11 @@ int gpt2b_gpu_sample_softmax(int* d_token, const float* logits, int B, int V, un
                              gpt2b_stream_t stream) {
     if (B <= 0 || V <= 0 || !d_token || !logits) return GPT2B_ERR_INVALID_ARG;
     return status_from(launch_k(sample_softmax_kernel, dim3(B), dim3(kSampThreads), 0, (cudaStream_t)stream, false, d_token, logits, B, V, seed, step));
+}
+
+int gpt2b_logits_nll(float* d_nll, const float* logits, int V, const int* d_token, gpt2b_stream_t stream) {
+    if (V <= 0 || !d_nll || !logits || !d_token) return GPT2B_ERR_INVALID_ARG;
+    return status_from(launch_nll(d_nll, logits, V, d_token, nullptr, nullptr, 0, (cudaStream_t)stream));
 }
 
 int gpt2b_gpu_argmax(int* d_token, const float* logits, int B, int V, int ld, gpt2b_stream_t stream) {

@@ -22,6 +22,11 @@ class _Config(ctypes.Structure):
                 ("num_layers", ctypes.c_int), ("num_heads", ctypes.c_int), ("channels", ctypes.c_int)]
 
 
+class _DumpConfig(ctypes.Structure):
+    _fields_ = [("dir", ctypes.c_char_p), ("prefix", ctypes.c_char_p), ("steps", ctypes.c_void_p),
+                ("n_steps", ctypes.c_int), ("ppl_len", ctypes.c_int), ("logits_t1", ctypes.c_int)]
+
+
 class Engine:
     """One decode engine on the current CUDA device."""
 
@@ -119,6 +124,25 @@ class Engine:
                                           logits.ctypes.data_as(ctypes.c_void_p) if want_logits else None,
                                           1 if sample else 0, seed), "gpt2b_engine_generate")
         return out, logits
+
+    def generate_dump(self, prompt, n_gen: int, dump_dir: str | None, prefix: str = "gpt2b", steps=(),
+                      ppl_len: int = 0, logits_t1: bool = True, sample: bool = False, seed: int = 1337):
+        """``generate`` with the reference's verification dumps
+        (Inference_gpt2/dump_utils.h file layout, written under ``dump_dir``):
+        step t's logits and input prefix for t in ``steps``, step 1's logits,
+        and the NLL of each appended token for steps 1..``ppl_len``
+        (computed on the device).  Returns (tokens[n_gen+1], nll[ppl_len])."""
+        prompt = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(n_gen + 1, np.int32)
+        nll = np.zeros(max(ppl_len, 1), np.float32)
+        st = np.ascontiguousarray(list(steps), dtype=np.int32)
+        cfg = _DumpConfig(dump_dir.encode() if dump_dir else None, prefix.encode(),
+                          st.ctypes.data if st.size else None, int(st.size), int(ppl_len), int(bool(logits_t1)))
+        check(lib().gpt2b_engine_generate_dump(self._h, prompt.ctypes.data_as(ctypes.c_void_p), len(prompt), n_gen,
+                                               out.ctypes.data_as(ctypes.c_void_p), 1 if sample else 0, seed,
+                                               ctypes.byref(cfg), nll.ctypes.data_as(ctypes.c_void_p)),
+              "gpt2b_engine_generate_dump")
+        return out, nll[:ppl_len]
 
     def set_position(self, token: int, pos: int) -> None:
         check(lib().gpt2b_engine_set_position(self._h, int(token), int(pos)), "gpt2b_engine_set_position")

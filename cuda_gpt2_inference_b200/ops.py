@@ -94,6 +94,48 @@ def attention_forward_kv_large(out, qkv, kv_cache, B, NH, hs, maxT, d_pos, part_
                  _p(part_lse), _p(part_max), S), "attention_forward_kv_large")
 
 
+def attention_kv_split(part_out, part_lse, part_max, qkv, kv_cache, B, NH, hs, maxT, S, d_pos, kv_scale=None,
+                       fmt=None, stream=None):
+    """The split half alone (attention_kv_split_kernel(_w8), attention_kvcache.cuh:185, _w8.cuh:260)."""
+    if kv_cache.dtype == torch.uint8:
+        fn = getattr(lib(), "gpt2b_attention_kv_split_w8_" + ("i8" if fmt == "int8" else "fp8"))
+        check(fn(_p(part_out), _p(part_lse), _p(part_max), _p(qkv), _p(kv_cache), _p(kv_scale), B, NH, hs, maxT, S,
+                 _p(d_pos), _s(stream)), "attention_kv_split_w8")
+    else:
+        fn = getattr(lib(), f"gpt2b_attention_kv_split_{_sfx(kv_cache)}")
+        check(fn(_p(part_out), _p(part_lse), _p(part_max), _p(qkv), _p(kv_cache), B, NH, hs, maxT, S, _p(d_pos),
+                 _s(stream)), "attention_kv_split")
+
+
+def attention_kv_merge(out, part_out, part_lse, part_max, B, NH, hs, S, w8=False, stream=None):
+    """The merge half alone (attention_kv_merge_kernel(_w8), attention_kvcache.cuh:298, _w8.cuh:374)."""
+    name = "gpt2b_attention_kv_merge_w8" if w8 else f"gpt2b_attention_kv_merge_{_sfx(out)}"
+    check(getattr(lib(), name)(_p(out), _p(part_out), _p(part_lse), _p(part_max), B, NH, hs, S, _s(stream)),
+          "attention_kv_merge")
+
+
+def matmul_forward(out, inp, weight, bias, B, T, C, OC, pre_gelu=None, scale=None, fmt=None, stream=None):
+    """out[B*T, OC] = inp . weight^T (+ bias), on the tensor cores
+    (matmul_forward_cublaslt, matmul.cuh:141).  BF16 inp; weight BF16 or 8-bit
+    codes (uint8 + per-row ``scale``, ``fmt`` "int8"/"fp8"); FP32 ``out``
+    selects the LM-head form (no bias); ``pre_gelu`` fuses tanh-GELU."""
+    w8 = weight.dtype == torch.uint8
+    sfx = ("i8" if fmt == "int8" else "fp8") if w8 else None
+    if out.dtype == torch.float32:
+        if w8:
+            rc = getattr(lib(), f"gpt2b_matmul_forward_w8_{sfx}_f32out")(_p(out), _p(inp), _p(weight), _p(scale), B, T,
+                                                                          C, OC, _s(stream))
+        else:
+            rc = lib().gpt2b_matmul_forward_f32out_bf16(_p(out), _p(inp), _p(weight), B, T, C, OC, _s(stream))
+    elif w8:
+        rc = getattr(lib(), f"gpt2b_matmul_forward_w8_{sfx}")(_p(out), _p(inp), _p(weight), _p(scale), _p(bias), B, T,
+                                                               C, OC, _p(pre_gelu), _s(stream))
+    else:
+        rc = lib().gpt2b_matmul_forward_bf16(_p(out), _p(inp), _p(weight), _p(bias), B, T, C, OC, _p(pre_gelu),
+                                             _s(stream))
+    check(rc, "matmul_forward")
+
+
 def layernorm_forward(out, mean, rstd, inp, weight, bias, B, T, C, stream=None):
     fn = getattr(lib(), f"gpt2b_layernorm_forward_{_sfx(inp)}")
     check(fn(_p(out), _p(mean), _p(rstd), _p(inp), _p(weight), _p(bias), B, T, C, _s(stream)), "layernorm_forward")

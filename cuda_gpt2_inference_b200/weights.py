@@ -39,10 +39,10 @@ def shapes(cfg: dict) -> dict:
     }
 
 
-def synth_params(cfg: dict, seed: int = 1234, init: str = "spec") -> dict:
-    """Seeded float32 parameters of the given architecture."""
+def param_stream(cfg: dict, seed: int = 1234, init: str = "spec"):
+    """Yield (name, float32 tensor) in file order, drawn one tensor at a time
+    (peak host memory: one tensor), for GPT-2-XL-sized models."""
     rng = np.random.default_rng(seed)
-    out = {}
     for name, shp in shapes(cfg).items():
         if name in LINEAR:
             a = rng.standard_normal(shp, dtype=np.float32) * np.float32(0.02)
@@ -56,9 +56,14 @@ def synth_params(cfg: dict, seed: int = 1234, init: str = "spec") -> dict:
             a = np.zeros(shp, np.float32)
             if init == "test":
                 a += rng.standard_normal(shp, dtype=np.float32) * np.float32(0.02)
-        out[name] = a
-    out["wte"][cfg["V"]:] = 0.0  # padded vocabulary rows are zero
-    return out
+        if name == "wte":
+            a[cfg["V"]:] = 0.0  # padded vocabulary rows are zero
+        yield name, a
+
+
+def synth_params(cfg: dict, seed: int = 1234, init: str = "spec") -> dict:
+    """Seeded float32 parameters of the given architecture."""
+    return dict(param_stream(cfg, seed, init))
 
 
 def bf16_bits(a: np.ndarray) -> np.ndarray:
@@ -100,24 +105,8 @@ def image_stream(cfg: dict, seed: int = 1234, init: str = "spec", dtype: str = "
     total = 1024 + sum(int(np.prod(v)) * eb for v in shp.values())
     out = np.empty(total, np.uint8)
     out[:1024] = np.frombuffer(header(cfg, 3 if dtype == "f32" else 5).tobytes(), np.uint8)
-    rng = np.random.default_rng(seed)
     off = 1024
-    for name in NAMES:  # the synth_params draw order (dict order of shapes() == NAMES)
-        sh = shp[name]
-        if name in LINEAR:
-            a = rng.standard_normal(sh, dtype=np.float32) * np.float32(0.02)
-        elif name == "wpe":
-            a = rng.standard_normal(sh, dtype=np.float32) * np.float32(0.01)
-        elif name.endswith("w"):
-            a = np.ones(sh, np.float32)
-            if init == "test":
-                a += rng.standard_normal(sh, dtype=np.float32) * np.float32(0.1)
-        else:
-            a = np.zeros(sh, np.float32)
-            if init == "test":
-                a += rng.standard_normal(sh, dtype=np.float32) * np.float32(0.02)
-        if name == "wte":
-            a[cfg["V"]:] = 0.0
+    for name, a in param_stream(cfg, seed, init):
         b = (np.ascontiguousarray(a) if dtype == "f32" else bf16_bits(a)).view(np.uint8).ravel()
         out[off:off + b.size] = b
         off += b.size

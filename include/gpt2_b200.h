@@ -185,6 +185,23 @@ int gpt2b_attention_kv_merge_bf16(uint16_t* out, const float* part_out, const fl
                                   const float* part_max, int B, int NH, int hs, int S, gpt2b_stream_t stream);
 int gpt2b_attention_kv_merge_f32(float* out, const float* part_out, const float* part_lse, const float* part_max,
                                  int B, int NH, int hs, int S, gpt2b_stream_t stream);
+/* FP32 split (attention_kvcache.cuh:185 in an FP32 build) and the 8-bit-KV
+ * halves launched raw by inference_gpt2_opt.cu:310-314:
+ * attention_kv_split_kernel_w8 (attention_kvcache_w8.cuh:260; codes x row scale,
+ * kv_scale as written by gpt2b_kv_cache_write_w8_*) and
+ * attention_kv_merge_kernel_w8 (attention_kvcache_w8.cuh:374; BF16 output, the
+ * same merge as gpt2b_attention_kv_merge_bf16). */
+int gpt2b_attention_kv_split_f32(float* part_out, float* part_lse, float* part_max, const float* qkv,
+                                 const float* kv_cache, int B, int NH, int hs, int maxT, int S, const int* d_pos,
+                                 gpt2b_stream_t stream);
+int gpt2b_attention_kv_split_w8_i8(float* part_out, float* part_lse, float* part_max, const uint16_t* qkv,
+                                   const uint8_t* kv_cache, const float* kv_scale, int B, int NH, int hs, int maxT,
+                                   int S, const int* d_pos, gpt2b_stream_t stream);
+int gpt2b_attention_kv_split_w8_fp8(float* part_out, float* part_lse, float* part_max, const uint16_t* qkv,
+                                    const uint8_t* kv_cache, const float* kv_scale, int B, int NH, int hs, int maxT,
+                                    int S, const int* d_pos, gpt2b_stream_t stream);
+int gpt2b_attention_kv_merge_w8(uint16_t* out, const float* part_out, const float* part_lse, const float* part_max,
+                                int B, int NH, int hs, int S, gpt2b_stream_t stream);
 /* No counterpart in the reference.  gpt2b_attention_forward_kv_large_bf16
  * without the three caller-provided partial buffers, for callers that cannot
  * allocate device memory (a host whose memory pool owns the whole device, or a
@@ -239,6 +256,40 @@ int gpt2b_gpu_sample_softmax(int* d_token, const float* logits, int B, int V, un
  * ties.  No counterpart in the reference (it only samples); the greedy decode
  * configurations need it. */
 int gpt2b_gpu_argmax(int* d_token, const float* logits, int B, int V, int ld, gpt2b_stream_t stream);
+/* *d_nll = log(sum_i exp(logits[i])) - logits[*d_token] over the first V
+ * logits (max-shifted, sum in double): the negative log-likelihood the
+ * reference's ppl_record_nll computes on the host after copying the logits
+ * back (Inference_gpt2/dump_utils.h:63-79), here on the device. */
+int gpt2b_logits_nll(float* d_nll, const float* logits, int V, const int* d_token, gpt2b_stream_t stream);
+
+/* ======================================================================== */
+/* Prompt GEMM on the tensor cores (tcgen05)                                */
+/* ======================================================================== */
+/* out[B*T x OC] = inp[B*T x C] . weight[OC x C]^T + bias, BF16 in and out,
+ * FP32 accumulation in tensor memory.  pre_gelu non-NULL: pre_gelu receives
+ * the pre-activation and out = gelu_tanh(pre).  Replaces
+ * matmul_forward_cublaslt (Inference_gpt2/matmul.cuh:141; the fused-GELU
+ * form, gelu_fusion >= 1).  inp and weight 16-byte aligned, C a multiple of 8. */
+int gpt2b_matmul_forward_bf16(uint16_t* out, const uint16_t* inp, const uint16_t* weight, const uint16_t* bias,
+                              int B, int T, int C, int OC, uint16_t* pre_gelu, gpt2b_stream_t stream);
+/* FP32 output, no bias (the LM head).  Replaces matmul_forward_cublaslt_f32
+ * (Inference_gpt2/matmul.cuh:158). */
+int gpt2b_matmul_forward_f32out_bf16(float* out, const uint16_t* inp, const uint16_t* weight, int B, int T, int C,
+                                     int OC, gpt2b_stream_t stream);
+/* 8-bit weight-only forms: weight = INT8 / E4M3 codes [OC x C] with one FP32
+ * scale per output row (quantize.cu format); out = gelu?(scale * (inp .
+ * codes^T) + bias).  No counterpart in the reference (its prompt path keeps
+ * BF16 weights); they run the prompt of the 8-bit engines.  C a multiple of 16. */
+int gpt2b_matmul_forward_w8_i8(uint16_t* out, const uint16_t* inp, const uint8_t* weight, const float* scale,
+                               const uint16_t* bias, int B, int T, int C, int OC, uint16_t* pre_gelu,
+                               gpt2b_stream_t stream);
+int gpt2b_matmul_forward_w8_fp8(uint16_t* out, const uint16_t* inp, const uint8_t* weight, const float* scale,
+                                const uint16_t* bias, int B, int T, int C, int OC, uint16_t* pre_gelu,
+                                gpt2b_stream_t stream);
+int gpt2b_matmul_forward_w8_i8_f32out(float* out, const uint16_t* inp, const uint8_t* weight, const float* scale,
+                                      int B, int T, int C, int OC, gpt2b_stream_t stream);
+int gpt2b_matmul_forward_w8_fp8_f32out(float* out, const uint16_t* inp, const uint8_t* weight, const float* scale,
+                                       int B, int T, int C, int OC, gpt2b_stream_t stream);
 
 /* ======================================================================== */
 /* Whole-model decode engine (replaces forward_kv_graph_ready,               */
@@ -257,12 +308,15 @@ enum {
     GPT2B_OPT_STEPS_PER_GRAPH = 4, /* decode steps captured into one graph (default 8) */
     GPT2B_OPT_PERSISTENT = 5, /* 1 (default where the shape allows): the whole decode loop runs in one
                                  cooperative kernel; 0: per-kernel steps (GEMV / attention launches) */
-    GPT2B_OPT_POLL_LIMIT = 6  /* persistent kernel: polls of one wait on another CTA (or another rank of a
+    GPT2B_OPT_POLL_LIMIT = 6, /* persistent kernel: polls of one wait on another CTA (or another rank of a
                                  tensor-parallel group) before it gives up, records
                                  GPT2B_DEVERR_GRID_TIMEOUT and makes every CTA of the group leave
                                  (default 4194304, a few seconds; at least 1024).  After a timeout in a
                                  tensor-parallel group the exchange words of the aborted call are
                                  stale: destroy and rebuild the group's engines. */
+    GPT2B_OPT_PREFILL = 7     /* 1 (default where the model allows: BF16 / 8-bit weights, single GPU): the
+                                 prompt of gpt2b_engine_generate (two tokens or more) runs as tensor-core
+                                 GEMMs over all its positions at once; 0: one decode step per position */
 };
 
 /* GPT2Config field order (Inference_gpt2/gpt2_model.h:28-35). */
@@ -311,6 +365,31 @@ int gpt2b_engine_forward(gpt2b_engine* e, int token, int pos);
  * gpt2b_gpu_sample_softmax(seed, step) instead of greedy. */
 int gpt2b_engine_generate(gpt2b_engine* e, const int* prompt, int n_prompt, int n_gen, int* out_tokens,
                           float* logits_host, int sample, unsigned long long seed);
+/* Verification dumps (Inference_gpt2/dump_utils.h; the --dump-steps,
+ * --dump-prefix and --ppl options of inference_gpt2_opt.cu:634-651).  Step t
+ * (t = 1 .. n_prompt + n_gen) is the forward at position t - 1; its "appended
+ * token" is the one at position t (teacher-forced from the prompt, then the
+ * greedy or sampled pick).  Files, in the reference's layout, under `dir`
+ * (created if missing):
+ *   <prefix>_logits_t1.bin            step 1's logits, V floats (logits_t1 != 0)
+ *   <prefix>_logits_step<t>.bin       step t's logits, V floats (t in steps[])
+ *   <prefix>_inputs_step<t>.bin       the tokens at positions 0..t-1, t ints
+ *   ppl_<prefix>_nll.bin              the NLL of each step's appended token, steps
+ *                                     1..ppl_len, floats (computed on the device)
+ *   ppl_<prefix>_tokens.bin           those tokens, ints
+ * dir NULL writes no files (nll_out still receives the NLLs). */
+typedef struct {
+    const char* dir;
+    const char* prefix;
+    const int* steps;
+    int n_steps;
+    int ppl_len;   /* 0: no NLL record */
+    int logits_t1;
+} gpt2b_dump_config;
+/* gpt2b_engine_generate (host buffers, one launch per step) with the dumps of
+ * `dump`.  nll_out (optional, host): ppl_len floats. */
+int gpt2b_engine_generate_dump(gpt2b_engine* e, const int* prompt, int n_prompt, int n_gen, int* out_tokens,
+                               int sample, unsigned long long seed, const gpt2b_dump_config* dump, float* nll_out);
 /* Device-resident decode: starting from the token and position already in the
  * engine's device slots, run n_steps greedy forwards without host round trips
  * (token and position advance on the device; picks are appended to the

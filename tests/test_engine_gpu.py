@@ -131,7 +131,27 @@ def test_persistent_launch_splits_bit_identical(mini, wmode, kvmode):
         eng.decode(n)
     hist = eng.history(len(prompt), 51)
     assert np.array_equal(hist, one_launch), (hist[:12], one_launch[:12])
+    # and the arithmetic of every step is independent of the call split: the last
+    # step's logits are bit-identical to those of the one-launch-per-step run
+    split_last = _device_logits(eng)
+    assert np.array_equal(split_last, lg[-1]), float(np.abs(split_last - lg[-1]).max())
+    eng.generate(prompt, 50)
+    assert np.array_equal(_device_logits(eng), lg[-1])
     eng.close()
+
+
+class _DevArray:
+    """A raw device pointer seen by torch (CUDA array interface)."""
+
+    def __init__(self, ptr, n):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 3}
+
+
+def _device_logits(eng):
+    import torch
+    torch.cuda.synchronize()
+    t = torch.as_tensor(_DevArray(eng.device_buffers()["logits"], eng.config["Vp"]), device="cuda")
+    return t.cpu().numpy().copy()
 
 
 def test_persistent_matches_kernel_path(mini):
@@ -228,6 +248,110 @@ def test_wide_model_extreme_activations(gpt2b, orc, cuda, wmode):
     m = orc.Model(img, wmode, "floatx", sc)
     cos_o = [cosine(lp[i], m.step(int(t), i)) for i, t in enumerate(seq)]
     assert min(cos_o) >= 0.999, min(cos_o)
+
+
+@pytest.mark.parametrize("wmode,kvmode", [("int8", "8bit"), ("fp8", "floatx"), ("bf16", "floatx")])
+def test_create_from_file_matches_buffer(mini, tmp_path, gpt2b, wmode, kvmode):
+    """gpt2b_engine_create_from_file on files written like the reference's
+    tools: the 8-bit image with its scales in "<model>_scales.bin" found
+    implicitly (inference_gpt2_opt.cu:666-668), or an explicit scale path; the
+    tokens and logits equal those of the engine built from the same bytes in
+    memory."""
+    from cuda_gpt2_inference_b200.engine import Engine
+    cfg, imgs = mini
+    img, sc = imgs[wmode]
+    model = tmp_path / "gpt2_mini.bin"
+    model.write_bytes(img)
+    if sc is not None:
+        (tmp_path / "gpt2_mini_scales.bin").write_bytes(sc.tobytes())
+    prompt = [4, 44, 444]
+    eb = _engine(img, wmode, kvmode, sc)
+    want_t, want_l = eb.generate(prompt, 20, want_logits=True)
+    eb.close()
+    ef = Engine.from_file(str(model), wmode, kvmode)  # implicit scale file
+    assert ef.config == dict(maxT=cfg["maxT"], V=cfg["V"], Vp=cfg["Vp"], L=cfg["L"], NH=cfg["NH"], C=cfg["C"])
+    got_t, got_l = ef.generate(prompt, 20, want_logits=True)
+    ef.close()
+    assert np.array_equal(got_t, want_t) and np.array_equal(got_l, want_l)
+    if sc is not None:
+        other = tmp_path / "elsewhere.bin"
+        other.write_bytes(sc.tobytes())
+        (tmp_path / "gpt2_mini_scales.bin").unlink()
+        with pytest.raises(gpt2b.Gpt2bError) as e:  # no implicit scale file any more
+            Engine.from_file(str(model), wmode, kvmode)
+        assert e.value.status == gpt2b.ERR_FILE
+        ef = Engine.from_file(str(model), wmode, kvmode, scale_path=str(other))
+        got_t, _ = ef.generate(prompt, 20)
+        ef.close()
+        assert np.array_equal(got_t, want_t)
+
+
+@pytest.mark.parametrize("path", PATHS)
+@pytest.mark.parametrize("sample", [False, True])
+def test_generate_dump_files(mini, tmp_path, path, sample):
+    """Verification dumps (Inference_gpt2/dump_utils.h layout): step 1's
+    logits, step t's logits and input prefix, and the per-step NLL of the
+    appended token computed on the device, against the logits and tokens of
+    gpt2b_engine_generate on the same engine and a host NLL."""
+    from cuda_gpt2_inference_b200 import verify
+    cfg, imgs = mini
+    img, _ = imgs["bf16"]
+    prompt = [50, 60, 70, 80]
+    n_gen, steps, ppl_len = 30, [1, 4, 5, 17, 34], 25
+    eng = _engine(img, "bf16", path=path)
+    want_t, lg = eng.generate(prompt, n_gen, want_logits=True, sample=sample, seed=99)
+    toks, nll = eng.generate_dump(prompt, n_gen, str(tmp_path), "opt_bf16", steps=steps, ppl_len=ppl_len,
+                                  sample=sample, seed=99)
+    eng.close()
+    assert np.array_equal(toks, want_t)
+    seq = np.array(list(prompt) + list(want_t), np.int32)  # the token at every position 0..n_prompt+n_gen
+    V = cfg["V"]
+    assert np.array_equal(verify.read_logits(str(tmp_path), "opt_bf16"), lg[0, :V])  # step 1
+    for t in steps:
+        assert np.array_equal(verify.read_logits(str(tmp_path), "opt_bf16", t), lg[t - 1, :V]), t
+        assert np.array_equal(verify.read_inputs(str(tmp_path), "opt_bf16", t), seq[:t]), t
+    fn, ft = verify.read_ppl(str(tmp_path), "opt_bf16")
+    assert np.array_equal(fn, nll) and np.array_equal(ft, seq[1:ppl_len + 1])
+    host = np.array([verify.nll(lg[t - 1, :V], int(seq[t])) for t in range(1, ppl_len + 1)], np.float32)
+    assert np.allclose(nll, host, rtol=1e-5, atol=1e-5)
+    assert verify.dumped_steps(str(tmp_path), "opt_bf16") == sorted(steps)
+
+
+@pytest.mark.parametrize("wmode,kvmode", [("bf16", "floatx"), ("int8", "8bit"), ("fp8", "8bit"), ("int8", "floatx")])
+@pytest.mark.parametrize("shape", ["mini", "long", "wide"])
+def test_prefill_matches_per_step_prompt(gpt2b, orc, cuda, wmode, kvmode, shape):
+    """The prompt on the tensor cores (one pass of tcgen05 GEMMs over every
+    prompt position) against the same prompt fed one decode step per position:
+    logits of every prompt position and of the decode steps that follow (which
+    read the KV rows the prefill wrote), teacher-forced on the same tokens, and
+    the first decode steps against the oracle.  "long": a 300-token prompt (three
+    128-row token tiles); "wide": C = 1600, 25 heads (the GPT-2-XL width)."""
+    from cuda_gpt2_inference_b200 import OPT_PREFILL, weights
+    cfg = {"mini": weights.mini_config(L=2, NH=2, maxT=64, V=500, Vp=512),
+           "long": weights.mini_config(L=1, NH=12, maxT=1024, V=500, Vp=512),
+           "wide": weights.mini_config(L=2, NH=25, maxT=128, V=500, Vp=512)}[shape]
+    n_prompt, n_gen = {"mini": (24, 30), "long": (300, 40), "wide": (24, 40)}[shape]
+    imgs = _images(gpt2b, cfg, 41, "test")
+    img, sc = imgs[wmode]
+    prompt = np.random.default_rng(8).integers(0, cfg["V"], n_prompt).astype(np.int32)
+    ep = _engine(img, wmode, kvmode, sc)
+    ep.set_option(OPT_PREFILL, 1)
+    toks, lp = ep.generate(prompt, n_gen, want_logits=True)
+    hist = ep.history(0, n_prompt)
+    ep.close()
+    assert np.array_equal(hist, prompt)  # the prompt is in the device history
+    seq = list(prompt) + list(toks[:-1])
+    es = _engine(img, wmode, kvmode, sc)
+    es.set_option(OPT_PREFILL, 0)
+    _, ls = es.generate(seq, 0, want_logits=True)
+    es.close()
+    cos = [cosine(lp[i], ls[i]) for i in range(len(seq))]
+    assert min(cos) >= 0.999, (min(cos), int(np.argmin(cos)))
+    # the pick after the prompt is the greedy pick of the last prompt row
+    assert int(toks[0]) == int(np.argmax(lp[n_prompt - 1][: cfg["V"]]))
+    m = orc.Model(img, wmode, kvmode, sc)
+    cos_o = [cosine(lp[i], m.step(int(t), i)) for i, t in enumerate(seq[: n_prompt + 4])]
+    assert min(cos_o) >= 0.999, (min(cos_o), int(np.argmin(cos_o)))
 
 
 def test_engine_rejects_bad_inputs(mini, gpt2b):

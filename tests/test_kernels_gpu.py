@@ -271,6 +271,60 @@ def test_attention_against_reference_kernels(cuda, orc, pos):
     assert checked == 2, "reference 8-bit kernels (INT8 and FP8) not built"
 
 
+@pytest.mark.parametrize("kind", ["f32", "bf16", "int8", "fp8"])
+@pytest.mark.parametrize("pos,S", [(0, 8), (150, 8), (700, 13), (1023, 8)])
+def test_attention_split_and_merge_halves(cuda, orc, kind, pos, S):
+    """The split and merge halves on their own: bit-identical to the combined
+    entry point (same kernels), and partials equal to the reference's own split
+    kernel (attention_kv_split_kernel / _w8) on the same cache."""
+    from cuda_gpt2_inference_b200 import ops
+    NH, hs, maxT = 12, 64, 1024
+    kvf, qkv = _kv_setup("bf16" if kind != "f32" else "f32", pos, 300 + pos)
+    dpos = torch.tensor([pos], dtype=torch.int32, device="cuda")
+    w8 = kind in ("int8", "fp8")
+    if w8:
+        codes = np.zeros((2, NH, maxT, hs), np.uint8)
+        scales = np.zeros((2, NH, maxT), np.float32)
+        for kvi in range(2):
+            for h in range(NH):
+                for j in range(pos + 1):
+                    codes[kvi, h, j], scales[kvi, h, j] = orc.kv_encode_row(kvf[kvi, h, j], kind)
+        cache, sc = dev(codes.ravel(), torch.uint8), dev(scales.ravel())
+        qd = dev(qkv, torch.bfloat16)
+        odt = torch.bfloat16
+    else:
+        dt = torch.float32 if kind == "f32" else torch.bfloat16
+        cache, sc, qd, odt = dev(kvf.ravel(), dt), None, dev(qkv, dt), dt
+    parts = [torch.zeros(NH * S * hs, device="cuda"), torch.zeros(NH * S, device="cuda"),
+             torch.zeros(NH * S, device="cuda")]
+    ops.attention_kv_split(*parts, qd, cache, 1, NH, hs, maxT, S, dpos, kv_scale=sc, fmt=kind)
+    half = torch.empty(NH * hs, device="cuda", dtype=odt)
+    ops.attention_kv_merge(half, *parts, 1, NH, hs, S, w8=w8)
+    whole = torch.empty(NH * hs, device="cuda", dtype=odt)
+    p2 = [torch.zeros_like(t) for t in parts]
+    ops.attention_forward_kv_large(whole, qd, cache, 1, NH, hs, maxT, dpos, *p2, S, kv_scale=sc, fmt=kind)
+    torch.cuda.synchronize()
+    assert torch.equal(half, whole)
+    lib = _ref_lib(orc, {"f32": "ops_f32", "bf16": "ops_bf16", "int8": "w8_int8", "fp8": "w8_fp8"}[kind])
+    if lib is None:
+        pytest.skip("reference kernels not built")
+    assert lib.ref_set_cur_len(pos) == 0
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    rp = [torch.zeros_like(t) for t in parts]
+    ro = torch.empty(NH * hs, device="cuda", dtype=odt)
+    if w8:
+        lib.ref_attention_split_merge_w8(vp(ro), vp(qd), vp(cache), vp(sc), 1, NH, hs, maxT, vp(rp[0]), vp(rp[1]),
+                                         vp(rp[2]), S)
+    else:
+        lib.ref_attention_split_merge(vp(ro), vp(qd), vp(cache), 1, NH, hs, maxT, vp(rp[0]), vp(rp[1]), vp(rp[2]), S)
+    torch.cuda.synchronize()
+    assert np.allclose(parts[2].cpu().numpy(), rp[2].cpu().numpy(), rtol=1e-5, atol=1e-5)  # split maxima
+    assert np.allclose(parts[1].cpu().numpy(), rp[1].cpu().numpy(), rtol=1e-4, atol=1e-6)  # split exp-sums
+    assert np.allclose(parts[0].cpu().numpy(), rp[0].cpu().numpy(), rtol=1e-3, atol=1e-4)  # un-normalised partials
+    tol = 1e-4 if kind == "f32" else 1e-2
+    assert rel_err(host(half), host(ro)) < tol
+
+
 # ------------------------------------------------------ LayerNorm etc. ----
 @pytest.mark.parametrize("C,N", [(768, 1), (768, 5), (1600, 1), (64, 3)])
 def test_layernorm_and_fused_residual(cuda, orc, C, N):
@@ -399,3 +453,47 @@ def test_quantize_file_matches_reference_tool(cuda, orc, tmp_path, gpt2b):
         assert q.ref_quantize_files(str(src).encode(), str(b8).encode(), str(bs).encode(), flag) == 0
         assert a8.read_bytes() == b8.read_bytes(), fmt
         assert as_.read_bytes() == bs.read_bytes(), fmt
+
+
+# ------------------------------------------------- prompt GEMM (tcgen05) ----
+MM_SHAPES = [(24, 768, 2304), (24, 3072, 768), (24, 768, 3072), (200, 768, 768), (5, 1600, 4800), (3, 776, 770),
+             (1, 64, 16)]
+
+
+@pytest.mark.parametrize("T,C,OC", MM_SHAPES)
+@pytest.mark.parametrize("fmt", ["bf16", "int8", "fp8"])
+def test_matmul_forward_tensor_cores(cuda, orc, T, C, OC, fmt):
+    """The tcgen05 prompt GEMM against a torch FP32 matmul of the same
+    BF16-rounded operands (8-bit: the dequantised codes x row scale): BF16
+    outputs within 1e-2 relative (bias, pre-GELU and fused GELU), FP32 outputs
+    within 1e-4.  Shapes cover several 128-row token tiles, N and K tails."""
+    from cuda_gpt2_inference_b200 import ops
+    if fmt != "bf16" and C % 16:
+        pytest.skip("8-bit rows must be a multiple of 16 bytes")
+    rng = np.random.default_rng(T * 7 + C + OC)
+    x = torch.from_numpy(rng.standard_normal((T, C), dtype=np.float32)).to(torch.bfloat16)
+    W = rng.standard_normal((OC, C), dtype=np.float32) * np.float32(0.02)
+    b = torch.from_numpy(rng.standard_normal(OC, dtype=np.float32) * np.float32(0.02)).to(torch.bfloat16)
+    if fmt == "bf16":
+        Wd = torch.from_numpy(W).to(torch.bfloat16)
+        Wref, sc = Wd.float(), None
+        Wdev = Wd.cuda()
+    else:
+        codes, scale = orc.quant_rows(W, fmt)
+        Wref = torch.from_numpy(orc.decode_w8(codes, fmt) * scale[:, None])
+        Wdev, sc = dev(codes, torch.uint8), dev(scale)
+    xd, bd = x.cuda(), b.cuda()
+    pre = x.float() @ Wref.t() + b.float()
+    out = torch.empty(T, OC, device="cuda", dtype=torch.bfloat16)
+    pg = torch.empty(T, OC, device="cuda", dtype=torch.bfloat16)
+    ops.matmul_forward(out, xd, Wdev, bd, 1, T, C, OC, pre_gelu=pg, scale=sc, fmt=fmt)
+    plain = torch.empty(T, OC, device="cuda", dtype=torch.bfloat16)
+    ops.matmul_forward(plain, xd, Wdev, bd, 1, T, C, OC, scale=sc, fmt=fmt)
+    o32 = torch.empty(T, OC, device="cuda")
+    ops.matmul_forward(o32, xd, Wdev, None, 1, T, C, OC, scale=sc, fmt=fmt)
+    torch.cuda.synchronize()
+    gelu = 0.5 * pre * (1 + torch.tanh(0.7978845608028654 * (pre + 0.044715 * pre ** 3)))
+    assert rel_err(host(pg), pre.numpy()) < 1e-2
+    assert rel_err(host(plain), pre.numpy()) < 1e-2
+    assert rel_err(host(out), gelu.numpy()) < 1e-2
+    assert rel_err(host(o32), (x.float() @ Wref.t()).numpy()) < 1e-4
