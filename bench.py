@@ -201,6 +201,31 @@ def time_launches(fn, flush=None, reps=20, warm=5):
     return statistics.median(s.elapsed_time(e) for s, e in evs[warm:])
 
 
+def graph_time(fn, n=20):
+    """ms per launch of n back-to-back launches captured in one CUDA graph (no
+    host launch latency, no other kernel in between; operands L2-warm)."""
+    import torch
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fn()
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(n):
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(200000)
+    s.record()
+    for _ in range(5):
+        g.replay()
+    e.record()
+    e.synchronize()
+    return s.elapsed_time(e) / (5 * n)
+
+
 def gemv_table(peak):
     """Standalone decode GEMVs (config-0 shapes): GB/s of algorithmic bytes,
     L2 flushed before each launch (cold) and with the operands L2-resident
@@ -230,10 +255,12 @@ def gemv_table(peak):
             fn()
             cold = time_launches(fn, flush)
             warm = time_launches(fn)
+            graph = graph_time(fn)
             gbs = nbytes / (cold * 1e-3) / 1e9
             res[f"{dt}_{M}x{K}"] = {"us": round(cold * 1e3, 2), "GB/s": round(gbs, 1), "frac": round(gbs / peak, 3),
                                     "warm_us": round(warm * 1e3, 2),
-                                    "warm_GB/s": round(nbytes / (warm * 1e-3) / 1e9, 1), "bytes": nbytes}
+                                    "warm_GB/s": round(nbytes / (warm * 1e-3) / 1e9, 1),
+                                    "graph_us": round(graph * 1e3, 2), "bytes": nbytes}
     del flush
     return res
 
@@ -766,9 +793,20 @@ def run_fp8_long(args):
 
 
 def run_profile_case(args):
-    """Three engine launches: 24-token prefill, decode to position 500, then
-    decode(8) -- the launch a profiler captures (-k <kernel> -s 2 -c 1 on the
-    persistent path)."""
+    """Small cases for profilers (ncu), one per --profile-case:
+    decode     the 24-token prompt (tensor-core prefill), decode to position
+               500, then decode(8): the persistent kernel's 2nd launch
+               (-k regex:decode_persistent -s 1 -c 1) is 8 steps at 500..507;
+    gemv       standalone GEMVs, per shape 2 launches after an L2 flush (cold)
+               then 2 back to back (warm): bf16 50257x768, int8 50257x768,
+               bf16 768x768, int8 768x768, bf16 2304x768 (20 gemv launches);
+    attention  12 heads x 64 at position 1023: split+merge (8 splits) then the
+               single-CTA form, BF16 KV then FP8 KV (flushed before each);
+    prefill    the 24-token prompt through the tensor-core GEMMs once."""
+    if args.profile_case == "gemv":
+        return profile_gemv()
+    if args.profile_case == "attention":
+        return profile_attention()
     import cuda_gpt2_inference_b200 as pkg
     from cuda_gpt2_inference_b200.engine import Engine
     if args.config == XL_CONFIG:  # one GPU
@@ -782,10 +820,69 @@ def run_profile_case(args):
         eng.set_option(pkg.OPT_PERSISTENT, 0)
     prompt = np.random.default_rng(24).integers(0, cfg["V"], PROMPT_LEN).astype(np.int32)
     eng.generate(prompt, 0)
-    eng.decode(500 - PROMPT_LEN)
-    eng.decode(8)
-    print("profile case done:", eng.history(500, 9)[:4].tolist())
+    if args.profile_case == "decode":
+        eng.decode(500 - PROMPT_LEN)
+        eng.decode(8)
+        print("profile case done:", eng.history(500, 9)[:4].tolist())
+    else:
+        print("profile case done:", eng.history(PROMPT_LEN, 1).tolist())
     eng.close()
+    return 0
+
+
+def profile_gemv():
+    import torch
+
+    from cuda_gpt2_inference_b200 import ops
+    torch.cuda.set_device(0)
+    flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    for dt, M, K in (("bf16", 50257, 768), ("int8", 50257, 768), ("bf16", 768, 768), ("int8", 768, 768),
+                     ("bf16", 2304, 768)):
+        out = torch.empty(M, device="cuda")
+        if dt == "int8":
+            W = torch.randint(0, 255, (M, K), dtype=torch.uint8, device="cuda")
+            sc, x = torch.rand(M, device="cuda"), torch.randn(K, device="cuda").to(torch.bfloat16)
+            fn = lambda: ops.launch_GEMV6_w8x2(out, None, W, x, sc, None, M, K, 0)  # noqa: E731
+        else:
+            W = (torch.randn(M, K, device="cuda") * 0.02).to(torch.bfloat16)
+            x = torch.randn(K, device="cuda").to(torch.bfloat16)
+            fn = lambda: ops.launch_GEMV6(out, W, x, M, K)  # noqa: E731
+        for _ in range(2):
+            flush.fill_(1)
+            fn()
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        print("gemv", dt, M, K, "done")
+    return 0
+
+
+def profile_attention():
+    import torch
+
+    from cuda_gpt2_inference_b200 import ops
+    torch.cuda.set_device(0)
+    NH, hs, maxT, S, pos = 12, 64, 1024, 8, 1023
+    flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    rng = np.random.default_rng(5)
+    d_pos = torch.tensor([pos], dtype=torch.int32, device="cuda")
+    po = torch.empty(NH * S * hs, device="cuda")
+    pl, pm = torch.empty(NH * S, device="cuda"), torch.empty(NH * S, device="cuda")
+    q = torch.from_numpy(rng.standard_normal(3 * NH * hs, dtype=np.float32)).to("cuda", torch.bfloat16)
+    out = torch.empty(NH * hs, device="cuda", dtype=torch.bfloat16)
+    kvf = torch.from_numpy(rng.standard_normal(2 * NH * maxT * hs, dtype=np.float32)).to("cuda", torch.bfloat16)
+    # E4M3 codes with no NaN pattern (exponent bits below 0x78), small row scales
+    cache8 = torch.randint(0, 255, (2 * NH * maxT * hs,), dtype=torch.uint8, device="cuda") & 0x77
+    sc8 = torch.rand(2 * NH * maxT, device="cuda") * 0.01
+    for kind, cache, sc in (("bf16", kvf, None), ("fp8", cache8, sc8)):
+        flush.fill_(1)
+        ops.attention_forward_kv_large(out, q, cache, 1, NH, hs, maxT, d_pos, po, pl, pm, S, kv_scale=sc,
+                                       fmt=None if sc is None else kind)
+        flush.fill_(2)
+        ops.attention_forward_kv_small(out, q, cache, 1, NH, hs, maxT, d_pos, kv_scale=sc,
+                                       fmt=None if sc is None else kind)
+    torch.cuda.synchronize()
+    print("attention done")
     return 0
 
 
@@ -801,9 +898,9 @@ def main():
     ap.add_argument("--quick", action="store_true",
                     help="skip the 1-GPU extras (other precisions, GEMV table, CPU and reference bars)")
     ap.add_argument("--no-xl", action="store_true", help="skip the GPT-2-XL tensor-parallel block")
-    ap.add_argument("--profile-case", action="store_true",
-                    help="small case for profilers: prefill, decode to position 500, then one 8-step decode "
-                         "(the 3rd engine launch); prints no bench line")
+    ap.add_argument("--profile-case", nargs="?", const="decode", default=None,
+                    choices=["decode", "gemv", "attention", "prefill"],
+                    help="small cases for profilers (see run_profile_case); prints no bench line")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
