@@ -467,7 +467,7 @@ cudaError_t setup_persistent(gpt2b_engine* e, int nsm) {
     int coop = 0;
     cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, e->device);
     const int S = std::min(nsm / NHl, persist_max_splits());
-    if (!coop || TP > 8 || !persist_supported(C, NHl, 64, maxT, S, nsm)) return cudaSuccess;
+    if (!coop || TP > 8 || !persist_supported(C, NHl, 64, maxT, S, nsm, L)) return cudaSuccess;
     const int kv_rows = engine_attn_chunk(maxT, S);
     int nsw = 0;
     const int kcap = std::max(2, std::min(persist_max_stages(), kPersistRingBytes / persist_stage_bytes(e->wk, C)));
@@ -489,12 +489,21 @@ cudaError_t setup_persistent(gpt2b_engine* e, int nsm) {
     const size_t own_words = n_qkv + n_att + n_part + n_fc;
     const size_t off_flags = align256(off_own + own_words * 8);
     const size_t flags = (size_t)L * NHl;
-    const size_t bytes = align256(off_flags + flags * 4) + 256;
+    const size_t off_epoch = align256(off_flags + flags * 4);  // the epoch counter (256 bytes)
+    const size_t off_lnexp = off_epoch + 256;                   // LayerNorm exponents (8-bit weights)
+    const size_t bytes = align256(off_lnexp + (2 * (size_t)L + 1) * 4);
     cudaError_t err = cudaMalloc(&e->xchg, bytes);
     if (err != cudaSuccess) return err;
     if ((err = cudaMemset(e->xchg, 0, bytes)) != cudaSuccess) return err;
     e->xchg_bytes = bytes;
     PersistParams& p = e->pp;
+    p.ln_exp = reinterpret_cast<const int*>(e->xchg + off_lnexp);
+    if (e->w8) {  // the tensor-core stages of 8-bit weights scale x by 2^-e before FP16
+        err = persist_ln_exponents(reinterpret_cast<int*>(e->xchg + off_lnexp), e->p[2], e->p[3], e->p[8], e->p[9],
+                                   e->p[14], e->p[15], L, C, nullptr);
+        if (err == cudaSuccess) err = cudaDeviceSynchronize();
+        if (err != cudaSuccess) return err;
+    }
     p.abort_flag = reinterpret_cast<int*>(e->xchg);
     p.ll_proj = reinterpret_cast<unsigned long long*>(e->xchg + off_proj);
     p.ll_fcproj = reinterpret_cast<unsigned long long*>(e->xchg + off_fcproj);
@@ -506,7 +515,7 @@ cudaError_t setup_persistent(gpt2b_engine* e, int nsm) {
     p.ll_part = w; w += n_part;
     p.ll_fc = w;
     p.kv_flag = reinterpret_cast<unsigned*>(e->xchg + off_flags);
-    p.d_epoch = reinterpret_cast<unsigned*>(e->xchg + align256(off_flags + flags * 4));
+    p.d_epoch = reinterpret_cast<unsigned*>(e->xchg + off_epoch);
     for (int r = 0; r < 8; r++) p.peer_x[r] = nullptr;
     p.peer_x[TP > 1 ? e->tp_rank : 0] = e->xchg;
     p.tp_rank = TP > 1 ? e->tp_rank : 0;

@@ -139,13 +139,21 @@ struct PersistParams {
     unsigned* d_epoch = nullptr;  // advanced by n_steps per call
     int* abort_flag = nullptr;    // zero at launch
     uint32_t poll_limit = 1u << 22;  // polls of one exchange wait before it gives up (GPT2B_OPT_POLL_LIMIT)
+    // 8-bit weights on tensor-core stages: per LayerNorm (LN1 and LN2 of layer l at 2l and 2l+1,
+    // the final LN at 2L) the exponent e with sqrt(C) max|gamma| + max|beta| < 2^(14+e), a bound
+    // of |x| (persist_ln_exponents)
+    const int* ln_exp = nullptr;
     float* logits = nullptr;      // Vp floats of the last step
     int n_steps = 0;
 };
 // exchange words between the (value, index) pairs of the LM-head pick: one CTA's
 // pair per 128-byte line (a line shared by several writers is slow to poll)
 constexpr int kPersistLmStride = 16;
-bool persist_supported(int C, int NH, int hs, int maxT, int splits, int nsm);
+bool persist_supported(int C, int NH, int hs, int maxT, int splits, int nsm, int L);
+// Fills out[2L+1] with the LayerNorm exponents of PersistParams::ln_exp from BF16 LayerNorm
+// parameters (ln1w/ln1b/ln2w/ln2b: L x C, lnfw/lnfb: C).
+cudaError_t persist_ln_exponents(int* out, const void* ln1w, const void* ln1b, const void* ln2w, const void* ln2b,
+                                 const void* lnfw, const void* lnfb, int L, int C, cudaStream_t st);
 int persist_max_splits();
 int persist_max_stages();
 int persist_stage_bytes(int wk, int C);  // one ring stage: 16 row-units of C weights + bias/scale tail

@@ -66,6 +66,7 @@ constexpr int kHSz = 64;              // head size
 constexpr int kMaxSplits = 32;        // attention splits per head
 constexpr int kMiscFloats = 128;      // reduction scratch, new-row codes and scales, stop flag
 constexpr int kXmaxSlot = 104;        // misc[104..111]: per-warp max |x| of a phase (8-bit tensor-core stages)
+constexpr int kMaxLayers = 127;       // layers of the persistent kernel (LayerNorm exponents in shared memory)
 constexpr int kGatherJ = 32;          // exchange words per consumer thread and gather (4C <= 8192)
 constexpr int kGatherJs = 16;         // the short gather (n <= 4096 words)
 enum { kPhQkv = 0, kPhProj = 1, kPhFc = 2, kPhFcproj = 3, kPhLm = 4 };
@@ -510,6 +511,20 @@ __device__ __forceinline__ void stage_mma(uint32_t a_base, const unsigned char* 
     s1 = d[2];
 }
 
+// x (activation type) -> FP16 scaled by 2^-e, e chosen so max |x| = am lands in [2^14, 2^15);
+// each thread rewrites its own channel pairs (2t, 2t+1) + 512j.  Returns 2^e.  Out of line:
+// rarely taken, and the per-layer code of the kernel is instruction-cache bound.
+template <typename XT>
+__device__ __noinline__ float rescale_x_fp16(const XT* xv, unsigned char* xh, int n, float am) {
+    const int e = am <= FLT_MAX ? ((__float_as_int(am) >> 23) & 0xff) - 127 - 14 : 100;
+    const int ec = max(-100, min(100, e));
+    const float x_down = __int_as_float((127 - ec) << 23);
+    for (int w = 2 * (int)threadIdx.x; w < n; w += 2 * kCT)
+        for (int k = 0; k < 2 && w + k < n; k++)
+            reinterpret_cast<__half*>(xh)[w + k] = __float2half_rn(to_f<XT>(xv[w + k]) * x_down);
+    return __int_as_float((127 + ec) << 23);
+}
+
 template <int KV>
 __device__ __forceinline__ float kv_code(uint32_t word, int j) {
     if constexpr (KV == KV_FP8) return e4m3_to_f(word, j);
@@ -531,7 +546,7 @@ __device__ __forceinline__ uint8_t kv_encode(float x, float scale) {
 // shared memory layout
 // ---------------------------------------------------------------------------
 struct PSmem {
-    int stage_bytes, ring, kvbuf, uni, res, lnp, red, xh, mred, misc, geo, bars, total;
+    int stage_bytes, ring, kvbuf, uni, res, lnp, red, xh, lnx, mred, misc, geo, bars, total;
 };
 
 template <int WK, int KV>
@@ -556,6 +571,7 @@ __host__ __device__ inline PSmem persist_layout(int C, int ns, int kv_rows, int 
     s.lnp = off; off += ((2 * C * xb) + 15) & ~15;  // LayerNorm gamma | beta of the current phase
     s.red = off; off += (tp > 1) ? tp * C * 4 : 0;  // every rank's projection partials
     s.xh = off; off += (wb == 1) ? 4 * C * 2 : 0;   // x as FP16, the B operand of 8-bit weights
+    s.lnx = off; off += (wb == 1) ? (2 * kMaxLayers + 2) * 4 : 0;  // LayerNorm exponents of 8-bit weights
     s.mred = off; off += 2 * kCW * 16 * 4;           // per-warp row sums of a stage, double-buffered
     s.misc = off; off += kMiscFloats * 4;
     s.geo = off; off += 5 * (int)sizeof(PhaseRows) + 4 * 8;  // this CTA's phase geometry, output bases
@@ -658,6 +674,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
     // paths read them from shared memory (no divisions or parameter loads there)
     PhaseRows* geo = reinterpret_cast<PhaseRows*>(sm + lay.geo);
     unsigned long long** obase = reinterpret_cast<unsigned long long**>(sm + lay.geo + 5 * sizeof(PhaseRows));
+    if constexpr (MMA && w8)  // the LayerNorm exponents, read once: global memory is far on the per-phase path
+        for (int i = tid; i <= 2 * L; i += kThreads) reinterpret_cast<int*>(sm + lay.lnx)[i] = P.ln_exp[i];
     if (tid < 5) {
         geo[tid] = phase_rows<MMA>(P, tid, b);
     } else if (tid < 9) {
@@ -824,13 +842,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                 const int l = lm ? 0 : (u >> 2);
                 const int ph = lm ? kPhLm : (u & 3);
                 XT* xv = reinterpret_cast<XT*>(xs);
-                // 8-bit tensor-core stages take x as FP16, scaled by 2^-e so that max |x| lands in
-                // [2^14, 2^15): no overflow for large activations, full precision for small ones;
-                // the row sums are multiplied back by 2^e (exact).  xmax: this thread's max |x|.
-                float xmax = 0.0f, x_up = 1.0f;
+                // 8-bit tensor-core stages take x as FP16 scaled by 2^-e, and the row sums are
+                // multiplied back by 2^e (exact): no overflow for large activations, full precision
+                // for small ones.  LayerNorm phases take e from a bound of |x| fixed by the LayerNorm
+                // parameters (P.ln_exp); the gather phases from the CTA's max |x| (xmax: this
+                // thread's part), combined on the barrier that follows the gather.
+                float xmax = 0.0f, x_up = 1.0f, x_down = 1.0f;
 
                 // ---------- x of this phase ----------
                 if (ph == kPhQkv || ph == kPhFc || lm) {
+                    int ln_e = 0;
+                    if constexpr (MMA && w8)
+                        ln_e = reinterpret_cast<const int*>(sm + lay.lnx)[lm ? 2 * L : 2 * l + (ph == kPhFc ? 1 : 0)];
                     // residual update (fcproj of the previous layer, or proj), then LayerNorm;
                     // gamma and beta are loaded (narrow: into registers; wide: bulk-copied into
                     // shared memory) while the inputs are awaited
@@ -940,6 +963,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                         ln_par ^= 1u;
                         ln_pending = false;
                     }
+                    if constexpr (MMA && w8) {
+                        x_down = __int_as_float((127 - ln_e) << 23);
+                        x_up = __int_as_float((127 + ln_e) << 23);
+                    }
 #pragma unroll
                     for (int j = 0; j < kCPT; j++) {
                         const int c = pair_slot(tid, j);
@@ -948,7 +975,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                             const float bb = WIDE ? to_f<XT>(lnp[C + c]) : lb[j];
                             const XT xvv = from_f<XT>((rstd * (res[c] - mean)) * g + bb);
                             xv[c] = xvv;
-                            if constexpr (MMA && w8) xmax = fmaxf(xmax, fabsf(to_f<XT>(xvv)));
+                            if constexpr (MMA && w8) reinterpret_cast<__half*>(xh)[c] = __float2half_rn(to_f<XT>(xvv) * x_down);
                         }
                     }
                 } else {
@@ -962,36 +989,28 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                         if (w < n) {
                             const XT xvv = from_f<XT>(gv[j]);
                             xv[w] = xvv;
-                            if constexpr (MMA && w8) xmax = fmaxf(xmax, fabsf(to_f<XT>(xvv)));
+                            if constexpr (MMA && w8) {  // FP16 as is: exact for |x| in [2^-14, 65504]
+                                xmax = fmaxf(xmax, fabsf(to_f<XT>(xvv)));
+                                reinterpret_cast<__half*>(xh)[w] = __float2half_rn(to_f<XT>(xvv));
+                            }
                         }
                     }
+                    if constexpr (MMA && w8) {
+                        xmax = warp_max(xmax);
+                        if (lane == 0) misc[kXmaxSlot + warp] = xmax;
+                    }
                     if (cta_any(!ok)) goto consumer_abort;
-                }
-                if constexpr (MMA && w8) {
-                    xmax = warp_max(xmax);
-                    if (lane == 0) misc[kXmaxSlot + warp] = xmax;
+                    if constexpr (MMA && w8) {
+                        // the CTA's max |x| (NaN entries are skipped by fmaxf and stay NaN): outside
+                        // [2^-4, 2^15] the FP16 copy is redone with x scaled into [2^14, 2^15) (rare;
+                        // kept compact, the per-layer code is instruction-cache bound)
+                        float am = misc[kXmaxSlot];
+#pragma unroll
+                        for (int w = 1; w < kCW; w++) am = fmaxf(am, misc[kXmaxSlot + w]);
+                        if (am > 32768.0f || (am > 0.0f && am < 0.0625f)) x_up = rescale_x_fp16(xv, xh, n, am);
+                    }
                 }
                 cta_sync();
-                if constexpr (MMA && w8) {
-                    // the CTA's max |x| (NaN entries are skipped by fmaxf and stay NaN), then each
-                    // warp converts the 32-value units of x its stage products read
-                    float am = misc[kXmaxSlot];
-#pragma unroll
-                    for (int w = 1; w < kCW; w++) am = fmaxf(am, misc[kXmaxSlot + w]);
-                    int e = 0;
-                    if (am > 0.0f) e = (am <= FLT_MAX) ? ((__float_as_int(am) >> 23) & 0xff) - 127 - 14 : 100;
-                    e = max(-100, min(100, e));
-                    const float x_down = __int_as_float((127 - e) << 23);
-                    x_up = __int_as_float((127 + e) << 23);
-                    const PhaseRows& pg = geo[ph];
-                    const int nku = pg.part >> 5;
-                    for (int kq = 0; kq < pg.kparts; kq++)
-                        for (int ku = warp; ku < nku; ku += kCW) {
-                            const int i = kq * pg.part + ku * 32 + lane;
-                            reinterpret_cast<__half*>(xh)[i] = __float2half_rn(to_f<XT>(xv[i]) * x_down);
-                        }
-                    __syncwarp();
-                }
                 PTRACE(u * 3 + 0);
 
                 // ---------- the matrix rows of this CTA ----------
@@ -1545,10 +1564,49 @@ int persist_smem_bytes(int wk, int kv, int C, int nsw, int kv_rows, int tp) {
     return s;
 }
 
-bool persist_supported(int C, int NH, int hs, int maxT, int splits, int nsm) {
+bool persist_supported(int C, int NH, int hs, int maxT, int splits, int nsm, int L) {
+    if (L > kMaxLayers) return false;
     if (hs != kHSz || C > kMaxC || C % 64 != 0 || (NH * maxT) % 4 != 0 || nsm > kMaxCtas) return false;
     if (splits < 1 || splits > kMaxSplits || NH * splits > nsm) return false;
     return engine_attn_chunk(maxT, splits) <= kMaxKvRows;
+}
+
+// One block per LayerNorm: the exponent e with B = sqrt(C) max|gamma| + max|beta| in
+// [2^(13+e), 2^(14+e)).  Since sum_c (r_c - mean)^2 = C var, every LayerNorm output obeys
+// |x_c| <= sqrt(C) |gamma_c| + |beta_c| <= B, so x 2^-e stays below 2^14 (a quarter of FP16's
+// range, margin for the rounding of the variance).
+__global__ void ln_exp_kernel(int* out, const __nv_bfloat16* ln1w, const __nv_bfloat16* ln1b,
+                              const __nv_bfloat16* ln2w, const __nv_bfloat16* ln2b, const __nv_bfloat16* lnfw,
+                              const __nv_bfloat16* lnfb, int L, int C) {
+    __shared__ float scratch[64];
+    const int i = blockIdx.x;
+    const __nv_bfloat16* w = i == 2 * L ? lnfw : ((i & 1) ? ln2w : ln1w) + (size_t)(i >> 1) * C;
+    const __nv_bfloat16* b = i == 2 * L ? lnfb : ((i & 1) ? ln2b : ln1b) + (size_t)(i >> 1) * C;
+    float gm = 0.0f, bm = 0.0f;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        gm = fmaxf(gm, fabsf(__bfloat162float(w[c])));
+        bm = fmaxf(bm, fabsf(__bfloat162float(b[c])));
+    }
+    gm = warp_max(gm);
+    bm = warp_max(bm);
+    if ((threadIdx.x & 31) == 0) { scratch[threadIdx.x >> 5] = gm; scratch[32 + (threadIdx.x >> 5)] = bm; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int k = 1; k < (int)(blockDim.x >> 5); k++) { gm = fmaxf(gm, scratch[k]); bm = fmaxf(bm, scratch[32 + k]); }
+        gm = fmaxf(gm, scratch[0]);
+        bm = fmaxf(bm, scratch[32]);
+        const float B = sqrtf((float)C) * gm + bm;
+        int e = 0;
+        if (B > 0.0f) e = (B <= FLT_MAX) ? ((__float_as_int(B) >> 23) & 0xff) - 127 - 13 : 100;
+        out[i] = max(-100, min(100, e));
+    }
+}
+
+cudaError_t persist_ln_exponents(int* out, const void* ln1w, const void* ln1b, const void* ln2w, const void* ln2b,
+                                 const void* lnfw, const void* lnfb, int L, int C, cudaStream_t st) {
+    using BF = __nv_bfloat16;
+    return launch_k(ln_exp_kernel, dim3(2 * L + 1), dim3(256), 0, st, false, out, (const BF*)ln1w, (const BF*)ln1b,
+                    (const BF*)ln2w, (const BF*)ln2b, (const BF*)lnfw, (const BF*)lnfb, L, C);
 }
 
 int persist_max_splits() { return kMaxSplits; }
