@@ -20,6 +20,13 @@
 //   * Each consumer warp takes a pair of rows (x read once per pair) and, when a
 //     tile has fewer than 16 rows, a slice of K.  FP32 accumulation; INT8 and
 //     E4M3 codes decode exactly with integer/bit operations (common.cuh).
+//   * Streamed 8-bit matrices (the LM head) go through the tensor cores instead:
+//     a warp tile is 16 rows copied row by row into a padded layout (ldmatrix
+//     without bank conflicts), the codes become exact FP16 pairs in registers,
+//     x is the B operand's column in FP16 after an exact power-of-two scaling
+//     of the CTA's max |x| into [2^14, 2^15), and mma.sync accumulates in FP32.
+//     About 25 warp instructions per 512 codes against ~3.5 per code per thread
+//     on the CUDA cores, which left the 8-bit stream instruction-bound.
 //   * Fused prologues for the engine: residual add + LayerNorm, embedding +
 //     LayerNorm, or the LSE merge of the attention split partials -- computed
 //     redundantly per CTA from a few KB of L2-resident data instead of separate
@@ -403,6 +410,9 @@ __device__ void lmhead_finish(const GemvParams& p, float best_v, int best_i, flo
     }
 }
 
+// Shared memory of the FP16 x copy (kernel B, tensor-core form).
+__host__ __device__ inline int mma_x_bytes(const GemvParams& p) { return p.mma ? p.K * 2 : 0; }
+
 // Bias / GELU / pre-GELU epilogue of one output row.
 template <typename XT, typename OT>
 __device__ __forceinline__ void store_row(const GemvParams& p, int row, float acc, float bias) {
@@ -569,13 +579,16 @@ __global__ void __launch_bounds__(kConsumers) gemv_stream_kernel(const GemvParam
     unsigned char* xs = smem + kSmemHeader;
     const int x_bytes = ((p.K * (int)sizeof(XT)) + 15) & ~15;
     unsigned char* aux = xs + x_bytes;
-    unsigned char* stages = aux + p.aux_bytes;
+    unsigned char* xh = aux + p.aux_bytes;  // FP16 x of the tensor-core form
+    unsigned char* stages = xh + mma_x_bytes(p);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const size_t row_bytes = (size_t)p.K * kWB;
+    const bool mma = k8 && p.mma;
     const int R = p.rows_per_tile, NSW = p.nstages;
+    const int RS = mma ? p.row_stride : (int)row_bytes;  // row pitch inside a tile
     const int LPR = 32 / R;  // lanes per row (R is a power of two <= 32)
-    const int rows_bytes_tile = (int)(((size_t)R * row_bytes + 15) & ~(size_t)15);
+    const int rows_bytes_tile = (int)(((size_t)R * RS + 15) & ~(size_t)15);
     const int gw = blockIdx.x * kConsumerWarps + warp, GW = gridDim.x * kConsumerWarps;
     const int my_tiles = (p.ntiles > gw) ? (p.ntiles - gw + GW - 1) / GW : 0;
     uint64_t* my_full = full + warp * kMaxWarpStages;
@@ -589,19 +602,27 @@ __global__ void __launch_bounds__(kConsumers) gemv_stream_kernel(const GemvParam
     }
     __syncthreads();
 
-    auto issue = [&](int k) {  // lane 0: stage warp tile k of this warp
+    // Stage warp tile k of this warp: one copy of the contiguous rows (lane 0),
+    // or in the tensor-core form one copy per row into the padded pitch (lane r
+    // copies row r; lane 0 arms the barrier first).  Called by the whole warp.
+    auto issue = [&](int k) {
         const int t = gw + k * GW;
         const int r0 = t * R, nr = min(R, p.M - r0);
         const int s = k % NSW;
         const uint32_t wbytes = (uint32_t)(nr * row_bytes);
         const uint32_t sbytes = p.scale_in_tile ? (uint32_t)(((nr + 3) & ~3) * 4) : 0u;
         unsigned char* st = my_stages + (size_t)s * p.tile_bytes;
-        mbar_arrive_expect_tx(&my_full[s], wbytes + sbytes);
-        bulk_g2s(st, Wb + (size_t)r0 * row_bytes, wbytes, &my_full[s]);
-        if (sbytes) bulk_g2s(st + rows_bytes_tile, p.scale + r0, sbytes, &my_full[s]);
+        if (lane == 0) mbar_arrive_expect_tx(&my_full[s], wbytes + sbytes);
+        if (mma) {
+            __syncwarp();
+            if (lane < nr) bulk_g2s(st + (size_t)lane * RS, Wb + (size_t)(r0 + lane) * row_bytes,
+                                    (uint32_t)row_bytes, &my_full[s]);
+        } else if (lane == 0) {
+            bulk_g2s(st, Wb + (size_t)r0 * row_bytes, wbytes, &my_full[s]);
+        }
+        if (lane == 0 && sbytes) bulk_g2s(st + rows_bytes_tile, p.scale + r0, sbytes, &my_full[s]);
     };
-    if (lane == 0)
-        for (int k = 0; k < NSW && k < my_tiles; k++) issue(k);
+    for (int k = 0; k < NSW && k < my_tiles; k++) issue(k);
 
     uint4 lw[kLnChunks], lb[kLnChunks];
     prefetch_ln_params<WK, PRO>(p, lw, lb);
@@ -609,16 +630,87 @@ __global__ void __launch_bounds__(kConsumers) gemv_stream_kernel(const GemvParam
     pdl_trigger();
     if (!build_x<WK, PRO>(p, xs, aux, aux_bar, misc, lw, lb)) return;
 
+    float x_up = 1.0f;
+    if (mma) {
+        // x -> FP16 x 2^-e with the CTA's max |x| in [2^14, 2^15): exact for every
+        // BF16 value down to 2^-29 of the maximum; row sums are scaled back by 2^e.
+        const XT* xv = reinterpret_cast<const XT*>(xs);
+        float am = 0.0f;
+        for (int k2 = tid; k2 < p.K; k2 += kConsumers) am = fmaxf(am, fabsf(to_f<XT>(xv[k2])));
+        am = warp_max(am);
+        if (lane == 0) misc[warp] = am;
+        consumer_sync();
+        am = misc[0];
+#pragma unroll
+        for (int w = 1; w < kConsumerWarps; w++) am = fmaxf(am, misc[w]);
+        int e = 0;
+        if (am > 0.0f && am <= FLT_MAX) e = max(-126, min(126, ((__float_as_int(am) >> 23) & 0xff) - 127 - 14));
+        const float x_down = __int_as_float((127 - e) << 23);
+        x_up = __int_as_float((127 + e) << 23);
+        __half2* xh2 = reinterpret_cast<__half2*>(xh);
+        for (int k2 = tid; 2 * k2 < p.K; k2 += kConsumers)
+            xh2[k2] = __floats2half2_rn(to_f<XT>(xv[2 * k2]) * x_down, to_f<XT>(xv[2 * k2 + 1]) * x_down);
+        consumer_sync();
+    }
+
     const int nch = (int)(row_bytes / 16);
     const int rr = lane / LPR, sub = lane % LPR;
     float best_v = -FLT_MAX;
     int best_i = 0x7fffffff;
+    // epilogue of one row: 8-bit scale, bias / GELU store or logits + running argmax
+    auto finish_row = [&](const unsigned char* tile, int r0, int r, float acc) {
+        const int row = r0 + r;
+        if constexpr (k8)
+            acc *= p.scale_in_tile ? reinterpret_cast<const float*>(tile + rows_bytes_tile)[r] : p.scale[row];
+        if constexpr (EPI == EPI_STORE) {
+            store_row<XT, OT>(p, row, acc, p.bias ? to_f<XT>(reinterpret_cast<const XT*>(p.bias)[row]) : 0.0f);
+        } else {
+            reinterpret_cast<float*>(p.out)[row] = acc;
+            if (row < p.vocab && acc > best_v) { best_v = acc; best_i = row; }
+        }
+    };
+    const uint32_t a_lane = (uint32_t)((lane & 15) * RS + (lane >> 4) * 16);  // ldmatrix row address of this lane
     for (int k = 0; k < my_tiles; k++) {
         const int s = k % NSW;
         if (!mbar_wait(&my_full[s], (uint32_t)((k / NSW) & 1))) return;
         const unsigned char* tile = my_stages + (size_t)s * p.tile_bytes;
         const int t = gw + k * GW;
         const int r0 = t * R, nr = min(R, p.M - r0);
+        if constexpr (k8) {
+            if (mma) {
+                // 16 rows x 32 codes per step: ldmatrix.x4 gives lane (g, q) bytes 4q..4q+3 of rows g
+                // and g + 8 in both 16-byte halves; two MMAs (one per half, separate accumulators)
+                // take x values 4q..4q+3 of the half as the B column.  Rows past nr hold stale
+                // bytes: their rows of D are discarded (a row of D depends on its row of A only).
+                float d0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, d1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                const uint32_t ab = smem_addr(tile) + a_lane;
+                const uint2* xw = reinterpret_cast<const uint2*>(xh) + (lane & 3);
+                const int nku = p.K >> 5;
+#pragma unroll 4
+                for (int ku = 0; ku < nku; ku++) {
+                    uint32_t q0, q1, q2, q3;
+                    ldsm_x4(ab + (uint32_t)ku * 32u, q0, q1, q2, q3);
+                    const uint2 x0 = xw[ku * 8], x1 = xw[ku * 8 + 4];
+                    mma_f16(d0, code2_to_f16x2<WK == WK_FP8>(q0, false), code2_to_f16x2<WK == WK_FP8>(q1, false),
+                            code2_to_f16x2<WK == WK_FP8>(q0, true), code2_to_f16x2<WK == WK_FP8>(q1, true), x0.x,
+                            x0.y);
+                    mma_f16(d1, code2_to_f16x2<WK == WK_FP8>(q2, false), code2_to_f16x2<WK == WK_FP8>(q3, false),
+                            code2_to_f16x2<WK == WK_FP8>(q2, true), code2_to_f16x2<WK == WK_FP8>(q3, true), x1.x,
+                            x1.y);
+                }
+                if ((lane & 3) == 0) {  // column 0 of D: rows g (d[0]) and g + 8 (d[2])
+                    const int g = lane >> 2;
+                    if (g < nr) finish_row(tile, r0, g, (d0[0] + d1[0]) * x_up);
+                    if (g + 8 < nr) finish_row(tile, r0, g + 8, (d0[2] + d1[2]) * x_up);
+                }
+                __syncwarp();
+                if (k + NSW < my_tiles) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // our reads before the refill
+                    issue(k + NSW);
+                }
+                continue;
+            }
+        }
         float acc0 = 0.0f, acc1 = 0.0f;
         if (rr < nr) {
             const unsigned char* wr = tile + (size_t)rr * row_bytes;
@@ -634,20 +726,10 @@ __global__ void __launch_bounds__(kConsumers) gemv_stream_kernel(const GemvParam
         }
         float acc = acc0 + acc1;
         for (int o = LPR / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (sub == 0 && rr < nr) {
-            const int row = r0 + rr;
-            if constexpr (k8)
-                acc *= p.scale_in_tile ? reinterpret_cast<const float*>(tile + rows_bytes_tile)[rr] : p.scale[row];
-            if constexpr (EPI == EPI_STORE) {
-                store_row<XT, OT>(p, row, acc, p.bias ? to_f<XT>(reinterpret_cast<const XT*>(p.bias)[row]) : 0.0f);
-            } else {
-                reinterpret_cast<float*>(p.out)[row] = acc;
-                if (row < p.vocab && acc > best_v) { best_v = acc; best_i = row; }
-            }
-        }
+        if (sub == 0 && rr < nr) finish_row(tile, r0, rr, acc);
         __syncwarp();
-        if (lane == 0 && k + NSW < my_tiles) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // our reads before the async refill
+        if (k + NSW < my_tiles) {
+            if (lane == 0) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // our reads before the refill
             issue(k + NSW);
         }
     }
@@ -660,7 +742,7 @@ __global__ void __launch_bounds__(kConsumers) gemv_stream_kernel(const GemvParam
 size_t gemv_smem_bytes(const GemvParams& p, int wk) {
     const size_t xb = (size_t)p.K * (wk == WK_F32 ? 4 : 2);
     const size_t rings = (size_t)(p.stream ? kConsumerWarps : 1) * p.nstages * p.tile_bytes;
-    return kSmemHeader + ((xb + 15) & ~(size_t)15) + (size_t)p.aux_bytes + rings;
+    return kSmemHeader + ((xb + 15) & ~(size_t)15) + (size_t)p.aux_bytes + mma_x_bytes(p) + rings;
 }
 
 // Streaming tuning knobs (read once): GPT2B_GEMV_TILE_KB (warp tile bytes of
@@ -675,6 +757,8 @@ static int env_int(const char* name, int dflt) {
 static const int g_tile_kb = env_int("GPT2B_GEMV_TILE_KB", 12);
 static const int g_stage_kb = env_int("GPT2B_GEMV_STAGE_KB", 100);
 static const int g_ctas_per_sm = env_int("GPT2B_GEMV_CTAS_PER_SM", 2);
+// GPT2B_GEMV_MMA=0 keeps streamed 8-bit matrices on the CUDA-core form (for A/B timing).
+static const int g_gemv_mma = env_int("GPT2B_GEMV_MMA", 1);
 
 bool plan_gemv(GemvParams& p, int wk, int nsm, bool single_wave) {
     const size_t row_bytes = (size_t)p.K * wkind_bytes(wk);
@@ -693,21 +777,38 @@ bool plan_gemv(GemvParams& p, int wk, int nsm, bool single_wave) {
         const size_t rows_b = ((size_t)r_even * row_bytes + 15) & ~(size_t)15;
         p.tile_bytes = (int)((rows_b + (p.scale_in_tile ? (size_t)r_even * 4 : 0) + 15) & ~(size_t)15);
     } else {
-        // kernel B: per-warp rings of R-row tiles, R a power of two <= 32
+        // kernel B: per-warp rings of R-row tiles, R a power of two <= 32; 8-bit codes
+        // with K a multiple of 32 take the tensor-core form (16-row tiles, rows padded to
+        // an odd number of 16-byte units so ldmatrix's 8 rows fall in distinct banks)
         p.stream = 1;
         int r = 1;
         while (r < 32 && (size_t)(2 * r) * row_bytes <= (size_t)g_tile_kb * 1024) r *= 2;
+        size_t pitch = row_bytes;
+        p.mma = 0;
+        if (w8 && g_gemv_mma && p.K % 32 == 0) {
+            const size_t rs = (row_bytes / 16) % 2 ? row_bytes : row_bytes + 16;
+            const size_t tile = ((16 * rs + 64) + 15) & ~(size_t)15;
+            if (kSmemHeader + 3 * (size_t)p.K + (size_t)p.aux_bytes + kConsumerWarps * tile + 1024 <=
+                (size_t)max_dyn_smem()) {
+                p.mma = 1;
+                r = 16;
+                pitch = rs;
+            }
+        }
+        p.row_stride = (int)pitch;
         p.rows_per_tile = r;
         p.ntiles = (p.M + r - 1) / r;
         p.scale_in_tile = (w8 && r % 4 == 0 && p.M % 4 == 0 && aligned16(p.scale)) ? 1 : 0;
-        const size_t rows_b = ((size_t)r * row_bytes + 15) & ~(size_t)15;
+        const size_t rows_b = ((size_t)r * pitch + 15) & ~(size_t)15;
         p.tile_bytes = (int)((rows_b + (p.scale_in_tile ? (size_t)r * 4 : 0) + 15) & ~(size_t)15);
-        const int warps_needed = p.ntiles;
-        p.grid = std::max(1, std::min(nsm * std::max(1, g_ctas_per_sm),
-                                      (warps_needed + kConsumerWarps - 1) / kConsumerWarps));
         const size_t budget = (size_t)g_stage_kb * 1024;
         p.nstages = (int)std::max<size_t>(1, std::min<size_t>(kMaxWarpStages, budget / ((size_t)kConsumerWarps *
                                                                                           p.tile_bytes)));
+        // CTAs per SM: the requested number, or as many as the SM's 228 KB of shared memory holds
+        const int fit = (int)(233472 / (gemv_smem_bytes(p, wk) + 1024));
+        const int cps = std::max(1, std::min(g_ctas_per_sm, fit));
+        const int warps_needed = p.ntiles;
+        p.grid = std::max(1, std::min(nsm * cps, (warps_needed + kConsumerWarps - 1) / kConsumerWarps));
     }
     p.x_vec = aligned16(p.x) ? 1 : 0;
     return true;

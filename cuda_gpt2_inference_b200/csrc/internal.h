@@ -47,6 +47,8 @@ struct GemvParams {
     int rows_per_tile = 0, ntiles = 0, nstages = 1, tile_bytes = 0, grid = 0;
     int stream = 0;               // 0: one tile per CTA (kernel A); 1: per-warp streaming rings (kernel B)
     int scale_in_tile = 0;        // 8-bit row scales travel with the weight tile
+    int mma = 0;                  // kernel B, 8-bit codes: 16-row tiles through mma.sync (x as scaled FP16)
+    int row_stride = 0;           // bytes between rows of a tile in shared memory (mma: padded)
     int x_vec = 0;                // x is 16-byte aligned (vector loads)
     int aux_bytes = 0;            // shared memory for PRO_ATTN_MERGE partials
     // PRO_RES_LN / PRO_EMB_LN

@@ -429,44 +429,10 @@ __device__ __forceinline__ void chunk_dot2(const uint4& w0, const uint4& w1, con
 // tensor-core stage products (mma.sync m16n8k16, FP32 accumulation): A = the
 // stage's 16 rows, B = x in column 0 (the other 7 columns zero)
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                 : "r"(addr));
-}
-__device__ __forceinline__ void mma_bf16(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                         uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-        "{%0, %1, %2, %3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void mma_f16(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                        uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-        "{%0, %1, %2, %3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-// Two codes of a 32-bit word (bytes 0-1 for hi = false, 2-3 for hi = true) as an
-// exact FP16 pair.  INT8: the sign-flipped byte under the FP16 exponent of 1024
-// reads 1024 + code + 128; subtracting 1152 leaves the code.  E4M3: the 7
-// magnitude bits placed as FP16 exponent/mantissa read 2^(e-15) x 1.m (or the
-// FP16 subnormal for e = 0); a multiply by 2^8 rebases the exponent.
+// Two codes of a 32-bit word as an exact FP16 pair (common.cuh: code2_to_f16x2).
 template <int WK>
 __device__ __forceinline__ uint32_t code2_f16x2(uint32_t word, bool hi) {
-    uint32_t r;
-    if constexpr (WK == WK_I8) {
-        const uint32_t h = __byte_perm(word ^ 0x80808080u, 0x64646464u, hi ? 0x4342u : 0x4140u);
-        asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(0x64806480u));
-    } else {
-        const uint32_t w = __byte_perm(word, 0u, hi ? 0x3424u : 0x1404u);  // bytes -> bits 8..15 / 24..31
-        const uint32_t f = (w & 0x80008000u) | ((w & 0x7f007f00u) >> 1);
-        asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(f), "r"(0x5c005c00u));
-    }
-    return r;
+    return code2_to_f16x2<WK == WK_FP8>(word, hi);
 }
 // This warp's share of a stage: 16-column blocks kb = warp, warp + 8, ...
 // (BF16) or 32-column units (8-bit: two MMAs per ldmatrix, the codes of an

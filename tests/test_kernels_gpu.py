@@ -104,6 +104,31 @@ def test_gemv6_w8x2(cuda, orc, fmt, M, K):
         assert rel_err(host(o), r) < 1e-2 and rel_err(host(p), rp) < 1e-2
 
 
+@pytest.mark.parametrize("fmt", ["int8", "fp8"])
+@pytest.mark.parametrize("M,K", [(50257, 768), (9999, 768), (5003, 1600), (9001, 784)])
+def test_gemv6_w8x2_streamed_forms(cuda, orc, fmt, M, K):
+    """Streamed 8-bit GEMVs (more rows than one tile per SM): the tensor-core form
+    (K a multiple of 32; 16-row tiles, ragged last tile at M = 9999 / 5003) and the
+    CUDA-core form (K = 784).  Against the oracle at 1e-5; x beyond FP16's range
+    (|x| ~ 1e5) and far below it (~1e-7) through the same exact power-of-two
+    scaling: out(x * 2^k) == out(x) * 2^k bit for bit."""
+    from cuda_gpt2_inference_b200 import ops
+    W, x, _ = _data(M, K, 7 * M + K)
+    codes, scale = orc.quant_rows(W, fmt)
+    Wd, sd = dev(codes, torch.uint8), dev(scale)
+    outs = {}
+    for k in (0, 17, -23):
+        x16 = orc.bf16_round(x * np.float32(2.0 ** k))
+        o = torch.empty(M, device="cuda")
+        ops.launch_GEMV6_w8x2(o, None, Wd, dev(x16, torch.bfloat16), sd, None, M, K, 0, fmt=fmt)
+        torch.cuda.synchronize()
+        outs[k] = host(o)
+        ref, _ = orc.gemv_w8(codes, fmt, x16, scale, None, 0)
+        assert rel_err(outs[k], ref) < 1e-5, k
+    assert np.array_equal(outs[17], outs[0] * np.float32(2.0 ** 17))
+    assert np.array_equal(outs[-23], outs[0] * np.float32(2.0 ** -23))
+
+
 @pytest.mark.parametrize("M,K", [(2304, 768), (3072, 768), (768, 3072), (50257, 768)])
 def test_gemv_against_reference_kernels(cuda, orc, M, K):
     """Our GEMVs vs the reference's GEMV6 / GEMV6_fused / GEMV6_w8x2 built for sm_100a."""
