@@ -21,7 +21,7 @@
 //     tile has fewer than 16 rows, a slice of K.  FP32 accumulation; INT8 and
 //     E4M3 codes decode exactly with integer/bit operations (common.cuh).
 //   * Streamed 8-bit matrices (the LM head) go through the tensor cores instead:
-//     a warp tile is 16 rows copied row by row into a padded layout (ldmatrix
+//     a warp tile is 16 rows copied as 8 row pairs into a padded layout (ldmatrix
 //     without bank conflicts), the codes become exact FP16 pairs in registers,
 //     x is the B operand's column in FP16 after an exact power-of-two scaling
 //     of the CTA's max |x| into [2^14, 2^15), and mma.sync accumulates in FP32.
@@ -586,9 +586,11 @@ __global__ void __launch_bounds__(kConsumers) gemv_stream_kernel(const GemvParam
     const size_t row_bytes = (size_t)p.K * kWB;
     const bool mma = k8 && p.mma;
     const int R = p.rows_per_tile, NSW = p.nstages;
-    const int RS = mma ? p.row_stride : (int)row_bytes;  // row pitch inside a tile
+    // pitch inside a tile: of rows, or in the tensor-core form of row pairs (rows 2p, 2p + 1
+    // adjacent, pairs padded to an odd number of 16-byte units)
+    const int RS = mma ? p.row_stride : (int)row_bytes;
     const int LPR = 32 / R;  // lanes per row (R is a power of two <= 32)
-    const int rows_bytes_tile = (int)(((size_t)R * RS + 15) & ~(size_t)15);
+    const int rows_bytes_tile = mma ? 8 * RS : (int)(((size_t)R * RS + 15) & ~(size_t)15);
     const int gw = blockIdx.x * kConsumerWarps + warp, GW = gridDim.x * kConsumerWarps;
     const int my_tiles = (p.ntiles > gw) ? (p.ntiles - gw + GW - 1) / GW : 0;
     uint64_t* my_full = full + warp * kMaxWarpStages;
@@ -603,8 +605,9 @@ __global__ void __launch_bounds__(kConsumers) gemv_stream_kernel(const GemvParam
     __syncthreads();
 
     // Stage warp tile k of this warp: one copy of the contiguous rows (lane 0),
-    // or in the tensor-core form one copy per row into the padded pitch (lane r
-    // copies row r; lane 0 arms the barrier first).  Called by the whole warp.
+    // or in the tensor-core form one copy per row pair into the padded pitch
+    // (lane p copies rows 2p and 2p + 1; lane 0 arms the barrier first).  Called
+    // by the whole warp.
     auto issue = [&](int k) {
         const int t = gw + k * GW;
         const int r0 = t * R, nr = min(R, p.M - r0);
@@ -615,8 +618,9 @@ __global__ void __launch_bounds__(kConsumers) gemv_stream_kernel(const GemvParam
         if (lane == 0) mbar_arrive_expect_tx(&my_full[s], wbytes + sbytes);
         if (mma) {
             __syncwarp();
-            if (lane < nr) bulk_g2s(st + (size_t)lane * RS, Wb + (size_t)(r0 + lane) * row_bytes,
-                                    (uint32_t)row_bytes, &my_full[s]);
+            if (2 * lane < nr)
+                bulk_g2s(st + (size_t)lane * RS, Wb + (size_t)(r0 + 2 * lane) * row_bytes,
+                         (uint32_t)(min(2, nr - 2 * lane) * row_bytes), &my_full[s]);
         } else if (lane == 0) {
             bulk_g2s(st, Wb + (size_t)r0 * row_bytes, wbytes, &my_full[s]);
         }
@@ -669,7 +673,10 @@ __global__ void __launch_bounds__(kConsumers) gemv_stream_kernel(const GemvParam
             if (row < p.vocab && acc > best_v) { best_v = acc; best_i = row; }
         }
     };
-    const uint32_t a_lane = (uint32_t)((lane & 15) * RS + (lane >> 4) * 16);  // ldmatrix row address of this lane
+    // ldmatrix row address of this lane: matrices 0 / 2 (A rows 0-7, bytes 0-15 / 16-31 of a
+    // 32-code step) are the even rows 2p, matrices 1 / 3 (A rows 8-15) the odd rows 2p + 1;
+    // the pair pitch puts the 8 rows of each matrix in distinct banks
+    const uint32_t a_lane = (uint32_t)((lane & 7) * RS + ((lane >> 3) & 1) * row_bytes + (lane >> 4) * 16);
     for (int k = 0; k < my_tiles; k++) {
         const int s = k % NSW;
         if (!mbar_wait(&my_full[s], (uint32_t)((k / NSW) & 1))) return;
@@ -678,10 +685,11 @@ __global__ void __launch_bounds__(kConsumers) gemv_stream_kernel(const GemvParam
         const int r0 = t * R, nr = min(R, p.M - r0);
         if constexpr (k8) {
             if (mma) {
-                // 16 rows x 32 codes per step: ldmatrix.x4 gives lane (g, q) bytes 4q..4q+3 of rows g
-                // and g + 8 in both 16-byte halves; two MMAs (one per half, separate accumulators)
-                // take x values 4q..4q+3 of the half as the B column.  Rows past nr hold stale
-                // bytes: their rows of D are discarded (a row of D depends on its row of A only).
+                // 16 rows x 32 codes per step: ldmatrix.x4 gives lane (g, q) bytes 4q..4q+3 of tile
+                // rows 2g (A row g) and 2g + 1 (A row g + 8) in both 16-byte halves; two MMAs (one
+                // per half, separate accumulators) take x values 4q..4q+3 of the half as the B
+                // column.  Rows past nr hold stale bytes: their rows of D are discarded (a row of
+                // D depends on its row of A only).
                 float d0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, d1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
                 const uint32_t ab = smem_addr(tile) + a_lane;
                 const uint2* xw = reinterpret_cast<const uint2*>(xh) + (lane & 3);
@@ -698,10 +706,10 @@ __global__ void __launch_bounds__(kConsumers) gemv_stream_kernel(const GemvParam
                             code2_to_f16x2<WK == WK_FP8>(q2, true), code2_to_f16x2<WK == WK_FP8>(q3, true), x1.x,
                             x1.y);
                 }
-                if ((lane & 3) == 0) {  // column 0 of D: rows g (d[0]) and g + 8 (d[2])
+                if ((lane & 3) == 0) {  // column 0 of D: tile rows 2g (d[0]) and 2g + 1 (d[2])
                     const int g = lane >> 2;
-                    if (g < nr) finish_row(tile, r0, g, (d0[0] + d1[0]) * x_up);
-                    if (g + 8 < nr) finish_row(tile, r0, g + 8, (d0[2] + d1[2]) * x_up);
+                    if (2 * g < nr) finish_row(tile, r0, 2 * g, (d0[0] + d1[0]) * x_up);
+                    if (2 * g + 1 < nr) finish_row(tile, r0, 2 * g + 1, (d0[2] + d1[2]) * x_up);
                 }
                 __syncwarp();
                 if (k + NSW < my_tiles) {
@@ -778,16 +786,17 @@ bool plan_gemv(GemvParams& p, int wk, int nsm, bool single_wave) {
         p.tile_bytes = (int)((rows_b + (p.scale_in_tile ? (size_t)r_even * 4 : 0) + 15) & ~(size_t)15);
     } else {
         // kernel B: per-warp rings of R-row tiles, R a power of two <= 32; 8-bit codes
-        // with K a multiple of 32 take the tensor-core form (16-row tiles, rows padded to
-        // an odd number of 16-byte units so ldmatrix's 8 rows fall in distinct banks)
+        // with K a multiple of 32 take the tensor-core form (16-row tiles copied as 8 row
+        // pairs, pairs padded to an odd number of 16-byte units so that the 8 rows of every
+        // ldmatrix fall in distinct banks)
         p.stream = 1;
         int r = 1;
         while (r < 32 && (size_t)(2 * r) * row_bytes <= (size_t)g_tile_kb * 1024) r *= 2;
         size_t pitch = row_bytes;
         p.mma = 0;
         if (w8 && g_gemv_mma && p.K % 32 == 0) {
-            const size_t rs = (row_bytes / 16) % 2 ? row_bytes : row_bytes + 16;
-            const size_t tile = ((16 * rs + 64) + 15) & ~(size_t)15;
+            const size_t rs = 2 * row_bytes + 16;  // row-pair pitch: an odd number of 16-byte units
+            const size_t tile = 8 * rs + 64;
             if (kSmemHeader + 3 * (size_t)p.K + (size_t)p.aux_bytes + kConsumerWarps * tile + 1024 <=
                 (size_t)max_dyn_smem()) {
                 p.mma = 1;
@@ -799,7 +808,7 @@ bool plan_gemv(GemvParams& p, int wk, int nsm, bool single_wave) {
         p.rows_per_tile = r;
         p.ntiles = (p.M + r - 1) / r;
         p.scale_in_tile = (w8 && r % 4 == 0 && p.M % 4 == 0 && aligned16(p.scale)) ? 1 : 0;
-        const size_t rows_b = ((size_t)r * pitch + 15) & ~(size_t)15;
+        const size_t rows_b = p.mma ? 8 * pitch : ((size_t)r * pitch + 15) & ~(size_t)15;
         p.tile_bytes = (int)((rows_b + (p.scale_in_tile ? (size_t)r * 4 : 0) + 15) & ~(size_t)15);
         const size_t budget = (size_t)g_stage_kb * 1024;
         p.nstages = (int)std::max<size_t>(1, std::min<size_t>(kMaxWarpStages, budget / ((size_t)kConsumerWarps *
