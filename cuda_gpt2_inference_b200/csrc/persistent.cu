@@ -160,6 +160,10 @@ __device__ __noinline__ void give_up(int* flag, const PeerSet* ps) {
                 asm volatile("st.relaxed.sys.global.b32 [%0], %1;" ::"l"(ps->x[r] + ps->off_abort), "r"(1) : "memory");
 }
 
+// Polls spin without a sleep: every iteration is already an L2 round trip, and a
+// __nanosleep(32) between polls measured 0.7 % (GPT-2 124M) to 3.3 % (GPT-2-XL)
+// slower per token.  The poll limit counts iterations (2^22 by default: seconds).
+//
 // Words i = tid + j*kCT (i < n, j < J) of src into out[j]; all loads of a
 // round are in flight together.  False on timeout (recorded) or abort.
 template <int J, bool SYS>
@@ -185,7 +189,6 @@ __device__ __noinline__ bool ll_gather_j(int* abort_flag, const PeerSet* ps, uin
         if (!pending) break;
         if (it > plim) { give_up(abort_flag, ps); return false; }
         if ((it & 15) == 15 && aborted(abort_flag)) return false;
-        __nanosleep(32);
     }
     return true;
 }
@@ -226,7 +229,6 @@ __device__ __noinline__ bool ll_gather2_j(int* abort_flag, const PeerSet* ps, ui
         if (!pending) break;
         if (it > plim) { give_up(abort_flag, ps); return false; }
         if ((it & 15) == 15 && aborted(abort_flag)) return false;
-        __nanosleep(32);
     }
     return true;
 }
@@ -272,7 +274,6 @@ __device__ __noinline__ bool ll_gather_pairs(int* abort_flag, const PeerSet* ps,
         if (!pending) break;
         if (it > plim) { give_up(abort_flag, ps); return false; }
         if ((it & 15) == 15 && aborted(abort_flag)) return false;
-        __nanosleep(32);
     }
     return true;
 }
@@ -1194,7 +1195,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                             if ((uint32_t)(w >> 32) == tag) { v = __uint_as_float((uint32_t)w); break; }
                             if (it > plim) { give_up(P.abort_flag, pgp); bad = true; break; }
                             if ((it & 15) == 15 && aborted(P.abort_flag)) { bad = true; break; }
-                            __nanosleep(32);
                         }
                         (tid < kHSz ? q_s : (tid < 2 * kHSz ? kcur : vcur))[tid & 63] = v;
                     }
