@@ -802,9 +802,14 @@ def run_profile_case(args):
                bf16 768x768, int8 768x768, bf16 2304x768 (20 gemv launches);
     attention  12 heads x 64 at position 1023: split+merge (8 splits) then the
                single-CTA form, BF16 KV then FP8 KV (flushed before each);
-    prefill    the 24-token prompt through the tensor-core GEMMs once."""
+    prefill    the 24-token prompt through the tensor-core GEMMs once;
+    trace      (needs the trace build: GPT2B_LIB=.../libgpt2b_trace.so) per-phase
+               times of the persistent kernel from its %globaltimer stamps, at
+               positions 24, 500 and 1000 (prints a JSON table)."""
     if args.profile_case == "gemv":
         return profile_gemv()
+    if args.profile_case == "trace":
+        return profile_trace(args)
     if args.profile_case == "attention":
         return profile_attention()
     import cuda_gpt2_inference_b200 as pkg
@@ -827,6 +832,75 @@ def run_profile_case(args):
     else:
         print("profile case done:", eng.history(PROMPT_LEN, 1).tolist())
     eng.close()
+    return 0
+
+
+def profile_trace(args):
+    """Phase times of the persistent kernel (trace build).  Thread 0 of every CTA
+    stamps %globaltimer when a phase's x is ready (gather / LayerNorm done), when
+    its rows are done and when its attention is done; CTA 0 stamps every stage
+    (producer issue, consumer wait start / end, done).  Decodes 4 steps from each
+    position and reports step 2: per-phase medians over CTAs, averaged over layers
+    (us)."""
+    import ctypes
+
+    import cuda_gpt2_inference_b200 as pkg
+    from cuda_gpt2_inference_b200.engine import Engine
+    lib = pkg.lib()
+    if not hasattr(lib, "gpt2b_persist_trace"):
+        raise SystemExit("--profile-case trace needs GPT2B_LIB pointing at libgpt2b_trace.so")
+    wmode, kvmode = CONFIGS[args.config]
+    cfg, _, img, sc = make_model(wmode, kvmode)
+    L = cfg["L"]
+    eng = Engine.from_buffer(img, wmode, kvmode, sc)
+    out = {}
+    for pos0 in (24, 500, 1000):
+        eng.set_position(7, pos0)
+        eng.decode(4)
+        eng.history(0, 1)
+        steps, ctas, evs = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        buf = (ctypes.c_ulonglong * (4 * 160 * 640))()
+        lib.gpt2b_persist_trace(buf, ctypes.byref(steps), ctypes.byref(ctas), ctypes.byref(evs))
+        tr = np.frombuffer(buf, dtype=np.uint64).reshape(steps.value, ctas.value, evs.value).astype(np.int64)
+        t = tr[2, :148]
+        start = t[:, evs.value - 1]
+        med = lambda a: float(np.median(a)) / 1000.0  # noqa: E731
+        acc = {k: [] for k in ("gather_ln1", "qkv", "attn", "gather_atty", "proj", "gather_ln2", "fc", "gather_fc",
+                               "fcproj")}
+        for l in range(L):
+            u = 4 * l
+            prev = t[:, 3 * (u - 1) + 1] if l > 0 else start
+            xr, rd, ad = t[:, 3 * u], t[:, 3 * u + 1], t[:, 3 * u + 2]
+            attn = ad > 0
+            acc["gather_ln1"].append(med(xr - prev))
+            acc["qkv"].append(med(rd - xr))
+            acc["attn"].append(med((ad - rd)[attn]))
+            acc["gather_atty"].append(med(t[:, 3 * (u + 1)] - np.where(attn, ad, rd)))
+            acc["proj"].append(med(t[:, 3 * (u + 1) + 1] - t[:, 3 * (u + 1)]))
+            acc["gather_ln2"].append(med(t[:, 3 * (u + 2)] - t[:, 3 * (u + 1) + 1]))
+            acc["fc"].append(med(t[:, 3 * (u + 2) + 1] - t[:, 3 * (u + 2)]))
+            acc["gather_fc"].append(med(t[:, 3 * (u + 3)] - t[:, 3 * (u + 2) + 1]))
+            acc["fcproj"].append(med(t[:, 3 * (u + 3) + 1] - t[:, 3 * (u + 3)]))
+        row = {k: round(float(np.mean(v)), 3) for k, v in acc.items()}
+        last = t[:, 3 * (4 * L - 1) + 1]
+        lm0, lm1, pick = t[:, 3 * 4 * L], t[:, 3 * 4 * L + 1], t[:, 3 * 4 * L + 2]
+        row.update(layer=round(med(last - start) / L, 3), lm_gather_ln=round(med(lm0 - last), 3),
+                   lm_rows=round(med(lm1 - lm0), 3), lm_pick=round(med(pick - lm1), 3),
+                   step=round(med(pick - start), 3))
+        sbuf = (ctypes.c_ulonglong * (2048 * 8))()
+        lib.gpt2b_persist_trace_stages(sbuf)
+        stg = np.frombuffer(sbuf, dtype=np.uint64).reshape(2048, 8).astype(np.int64)
+        ok = (stg[:, :4] > 0).all(axis=1) & (stg[:, 3] >= stg[:, 1]) & (stg[:, 1] > stg[:, 0] - 10 ** 7)
+        lmr = stg[:, 4] > 0  # LM-head rounds (two stages each) carry a fifth stamp
+        for name, sel in (("stage", ok & ~lmr), ("lm_round", ok & lmr)):
+            v = stg[sel]
+            if len(v):
+                row.update({f"{name}_lead": round(med(v[:, 1] - v[:, 0]), 3),
+                            f"{name}_wait": round(med(v[:, 2] - v[:, 1]), 3),
+                            f"{name}_compute": round(med(v[:, 3] - v[:, 2]), 3)})
+        out[pos0] = row
+    eng.close()
+    print(json.dumps({"config": args.config, "unit": "us", "phases": out}, indent=1))
     return 0
 
 
@@ -899,7 +973,7 @@ def main():
                     help="skip the 1-GPU extras (other precisions, GEMV table, CPU and reference bars)")
     ap.add_argument("--no-xl", action="store_true", help="skip the GPT-2-XL tensor-parallel block")
     ap.add_argument("--profile-case", nargs="?", const="decode", default=None,
-                    choices=["decode", "gemv", "attention", "prefill"],
+                    choices=["decode", "gemv", "attention", "prefill", "trace"],
                     help="small cases for profilers (see run_profile_case); prints no bench line")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -18,7 +18,8 @@ import os
 import re
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libgpt2b.so")
+# GPT2B_LIB selects another build of the library (the trace build of the build script)
+LIB_PATH = os.environ.get("GPT2B_LIB") or os.path.join(_HERE, "libgpt2b.so")
 HEADER_PATH = os.path.join(os.path.dirname(_HERE), "include", "gpt2_b200.h")
 
 # status codes (include/gpt2_b200.h)
@@ -123,6 +124,11 @@ _SIGS = {
     "gpt2b_engine_tp_ipc_handle": (_I, [_P, _P]),
     "gpt2b_engine_tp_connect": (_I, [_P, _P, _I]),
 }
+# only in the trace build
+_TRACE_SIGS = {
+    "gpt2b_persist_trace": (_I, [_P, _P, _P, _P]),
+    "gpt2b_persist_trace_stages": (_I, [_P]),
+}
 
 _lib = None
 
@@ -147,6 +153,10 @@ def lib() -> ctypes.CDLL:
             fn = getattr(dll, name)
             fn.restype = res
             fn.argtypes = args
+        for name, (res, args) in _TRACE_SIGS.items():
+            if hasattr(dll, name):
+                getattr(dll, name).restype = res
+                getattr(dll, name).argtypes = args
         _lib = dll
     return _lib
 

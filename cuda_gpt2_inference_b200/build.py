@@ -6,7 +6,11 @@ arch=compute_100a,code=sm_100a -lineinfo -O3 --use_fast_math``) into
 reference build (Makefile:137) so fast-math divisions in the quantisers give
 the reference's bytes.  Objects go to ``cuda_gpt2_inference_b200/_build/``.
 
-Usage: ``python -m cuda_gpt2_inference_b200.build [--force] [--verbose]``.
+Usage: ``python -m cuda_gpt2_inference_b200.build [--force] [--verbose] [--trace]``.
+``--trace`` builds ``libgpt2b_trace.so`` instead (objects in ``_build_trace/``): the
+persistent kernel stamps ``%globaltimer`` at its phase boundaries
+(``GPT2B_PERSIST_TRACE``; ``bench.py --profile-case trace`` reads them).  Load it with
+``GPT2B_LIB=<path>``.
 """
 from __future__ import annotations
 
@@ -21,6 +25,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OBJ = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libgpt2b.so")
+OBJ_TRACE = os.path.join(HERE, "_build_trace")
+LIB_TRACE = os.path.join(HERE, "libgpt2b_trace.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
@@ -56,16 +62,20 @@ def _headers():
         glob.glob(os.path.join(INCLUDE, "*.h"))
 
 
-def build(force: bool = False, verbose: bool = False, jobs: int | None = None, ptxas_info: bool = False) -> str:
-    """Compile csrc/*.cu into libgpt2b.so (incremental) and return its path."""
-    os.makedirs(OBJ, exist_ok=True)
+def build(force: bool = False, verbose: bool = False, jobs: int | None = None, ptxas_info: bool = False,
+          trace: bool = False) -> str:
+    """Compile csrc/*.cu into libgpt2b.so (or the trace build) incrementally and return its path."""
+    obj_dir, lib = (OBJ_TRACE, LIB_TRACE) if trace else (OBJ, LIB)
+    os.makedirs(obj_dir, exist_ok=True)
     srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
     hdr_t = max((os.path.getmtime(h) for h in _headers()), default=0.0)
     nccl_inc, nccl_lib = _nccl_paths()
     extra = [f"-I{nccl_inc}", "-DGPT2B_HAVE_NCCL=1"] if nccl_inc else []
+    if trace:
+        extra.append("-DGPT2B_PERSIST_TRACE=1")
     objs, work = [], []
     for s in srcs:
-        o = os.path.join(OBJ, os.path.basename(s)[:-3] + ".o")
+        o = os.path.join(obj_dir, os.path.basename(s)[:-3] + ".o")
         objs.append(o)
         if force or not os.path.exists(o) or os.path.getmtime(o) < max(os.path.getmtime(s), hdr_t,
                                                                          os.path.getmtime(__file__)):
@@ -78,12 +88,12 @@ def build(force: bool = False, verbose: bool = False, jobs: int | None = None, p
     if ptxas_info:
         for o in outs:
             print(o)
-    if work or force or not os.path.exists(LIB):
-        link = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart"]
+    if work or force or not os.path.exists(lib):
+        link = [NVCC, *ARCH, "-shared", "-o", lib, *objs, "-lcudart"]
         if nccl_lib:
             link += [f"-L{nccl_lib}", "-l:libnccl.so.2", f"-Xlinker=-rpath,{nccl_lib}"]
         _run(link, verbose)
-    return LIB
+    return lib
 
 
 def main() -> int:
@@ -91,8 +101,9 @@ def main() -> int:
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
     ap.add_argument("--ptxas-info", action="store_true", help="print -Xptxas -v register/spill/smem usage")
+    ap.add_argument("--trace", action="store_true", help="build libgpt2b_trace.so (persistent-kernel phase stamps)")
     a = ap.parse_args()
-    print(build(a.force, a.verbose, ptxas_info=a.ptxas_info))
+    print(build(a.force, a.verbose, ptxas_info=a.ptxas_info, trace=a.trace))
     return 0
 
 

@@ -77,12 +77,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return done != 0;
 }
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 // Bounded wait on an mbarrier phase.  Returns false (and records
-// GPT2B_DEVERR_MBAR_TIMEOUT) when the phase never completes.
+// GPT2B_DEVERR_MBAR_TIMEOUT) when the phase does not complete within about
+// two seconds (a try_wait may suspend the thread for a while, so the bound is
+// taken on %globaltimer, with an iteration cap behind it).
 constexpr uint32_t kMbarSpinLimit = 1u << 24;
+constexpr uint64_t kMbarTimeoutNs = 2000000000ull;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    for (uint32_t i = 0; i < kMbarSpinLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 0; i < kMbarSpinLimit; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255) == 255 && global_ns() - t0 > kMbarTimeoutNs) break;
+    }
     report_device_error(GPT2B_DEVERR_MBAR_TIMEOUT);
     return false;
 }

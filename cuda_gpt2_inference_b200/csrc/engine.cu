@@ -469,13 +469,20 @@ cudaError_t setup_persistent(gpt2b_engine* e, int nsm) {
     const int S = std::min(nsm / NHl, persist_max_splits());
     if (!coop || TP > 8 || !persist_supported(C, NHl, 64, maxT, S, nsm, L)) return cudaSuccess;
     const int kv_rows = engine_attn_chunk(maxT, S);
+    // ring: as many stages as fit in shared memory (the LM head streams through all of
+    // them); the layer phases run at most kPersistRingBytes of weights ahead (a deeper
+    // look-ahead there only adds traffic while the CTAs wait on exchange words).  The
+    // narrow kernels with 8-bit weights keep the ring at that depth: their LM head
+    // measured 9-12 % slower per token with 14 stages than with 8 (BF16 narrow, 4 -> 7
+    // stages: -0.7 %; GPT-2-XL wide: -2 %)
     int nsw = 0;
-    const int kcap = std::max(2, std::min(persist_max_stages(), kPersistRingBytes / persist_stage_bytes(e->wk, C)));
-    for (int k = kcap; k >= 2 && !nsw; k--) {
+    for (int k = persist_max_stages(); k >= 2 && !nsw; k--) {
         const int b = persist_smem_bytes(e->wk, e->kvk, C, k, kv_rows, TP);
         if (b > 0 && b <= max_dyn_smem()) nsw = k;
     }
     if (!nsw) return cudaSuccess;
+    const int lookahead = std::max(2, std::min(nsw, kPersistRingBytes / persist_stage_bytes(e->wk, C)));
+    if (e->w8 && persist_narrow(C, kv_rows, TP)) nsw = lookahead;
     const int G = nsm;
     const int Q = 3 * NHl * 64, A = NHl * 64, F = e->f_l;
     // exchange arena: the cross-GPU parts first, at offsets every rank shares
@@ -521,7 +528,7 @@ cudaError_t setup_persistent(gpt2b_engine* e, int nsm) {
     p.tp_rank = TP > 1 ? e->tp_rank : 0;
     p.tp_size = TP;
     p.C = C; p.L = L; p.NH = NHl; p.V = c.vocab_size; p.Vp = c.padded_vocab_size; p.maxT = maxT;
-    p.splits = S; p.nsw = nsw; p.G = G; p.kv_rows = kv_rows;
+    p.splits = S; p.nsw = nsw; p.G = G; p.kv_rows = kv_rows; p.lookahead = lookahead;
     p.qkv_rows = Q; p.proj_k = A; p.fc_rows = F; p.fcproj_k = F; p.v_rows = e->v_rows; p.v0 = e->v0;
     p.attn_scale = 1.0f / sqrtf(64.0f);
     p.W[0] = e->p[0]; p.W[1] = e->p[4]; p.W[2] = e->p[6]; p.W[3] = e->p[10]; p.W[4] = e->p[12];

@@ -108,6 +108,7 @@ cudaError_t launch_nll(float* out, const float* logits, int V, const int* tok, c
 struct PersistParams {
     int C = 0, L = 0, NH = 0, V = 0, Vp = 0, maxT = 0, splits = 0, nsw = 0, G = 0;
     int kv_rows = 0;  // positions one attention CTA stages (the largest chunk at maxT)
+    int lookahead = 0;  // stages the producer runs ahead in the layer phases (the LM head uses all nsw)
     // this rank's matrix shapes (single GPU: 3C, C, 4C, 4C, Vp, 0) and tensor-parallel group;
     // NH above is this rank's head count
     int qkv_rows = 0, proj_k = 0, fc_rows = 0, fcproj_k = 0, v_rows = 0, v0 = 0;
@@ -158,6 +159,7 @@ cudaError_t persist_ln_exponents(int* out, const void* ln1w, const void* ln1b, c
                                  const void* lnfw, const void* lnfb, int L, int C, cudaStream_t st);
 int persist_max_splits();
 int persist_max_stages();
+bool persist_narrow(int C, int kv_rows, int tp);  // the launch takes the narrow (CUDA-core) kernel
 int persist_stage_bytes(int wk, int C);  // one ring stage: 16 row-units of C weights + bias/scale tail
 // Weight bytes the ring holds at most: deeper look-ahead measured slower on B200 (GPT-2 124M:
 // 4 BF16 / 8 INT8 stages beat the 7 / 14 that fit; the extra copies only add HBM traffic

@@ -303,6 +303,9 @@ __device__ __forceinline__ void best_merge(float& bv, int& bi, float ov, int oi)
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
+__device__ __forceinline__ void mbar_arrive_cnt(uint64_t* bar, uint32_t n) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(n) : "memory");
+}
 
 // ---------------------------------------------------------------------------
 // phases
@@ -478,6 +481,51 @@ __device__ __forceinline__ void stage_mma(uint32_t a_base, const unsigned char* 
     s1 = d[2];
 }
 
+// One LM-head stage by one warp on the tensor cores (narrow kernels): 16 rows stored as
+// row pairs (rows 2p, 2p + 1 adjacent at pitch 2 x row + 16 bytes, so the 8 rows of every
+// ldmatrix fall in distinct banks; ldmatrix rows 0-7 are the even rows, 8-15 the odd
+// ones) times x over all K columns, two accumulator chains.  BF16 rows take x as BF16;
+// 8-bit codes become exact FP16 pairs against x as FP16 (xb = the scaled copy).  Returns,
+// for lanes with (lane & 3) == 0, the sums of stage rows 2(lane/4) (s0) and 2(lane/4) + 1 (s1).
+template <int WK>
+__device__ __forceinline__ void lm_stage_mma(uint32_t a, const unsigned char* xb, int K, int lane, float& s0,
+                                             float& s1) {
+    float d0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, d1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if constexpr (WK == WK_BF16) {
+        float d2[4] = {0.0f, 0.0f, 0.0f, 0.0f}, d3[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        const uint32_t* xw = reinterpret_cast<const uint32_t*>(xb) + (lane & 3);
+        const int nkb = K >> 4;  // 16-column blocks (K a multiple of 64: whole groups of 4)
+        for (int kb = 0; kb < nkb; kb += 4) {
+            uint32_t a0, a1, a2, a3, c0, c1, c2, c3, e0, e1, e2, e3, f0, f1, f2, f3;
+            ldsm_x4(a + (uint32_t)kb * 32u, a0, a1, a2, a3);
+            ldsm_x4(a + (uint32_t)kb * 32u + 32u, c0, c1, c2, c3);
+            ldsm_x4(a + (uint32_t)kb * 32u + 64u, e0, e1, e2, e3);
+            ldsm_x4(a + (uint32_t)kb * 32u + 96u, f0, f1, f2, f3);
+            mma_bf16(d0, a0, a1, a2, a3, xw[kb * 8], xw[kb * 8 + 4]);
+            mma_bf16(d1, c0, c1, c2, c3, xw[kb * 8 + 8], xw[kb * 8 + 12]);
+            mma_bf16(d2, e0, e1, e2, e3, xw[kb * 8 + 16], xw[kb * 8 + 20]);
+            mma_bf16(d3, f0, f1, f2, f3, xw[kb * 8 + 24], xw[kb * 8 + 28]);
+        }
+        d0[0] += d2[0]; d0[2] += d2[2];
+        d1[0] += d3[0]; d1[2] += d3[2];
+    } else {
+        const uint2* xw = reinterpret_cast<const uint2*>(xb) + (lane & 3);
+        const int nku = K >> 5;  // 32-code units
+#pragma unroll 2
+        for (int ku = 0; ku < nku; ku++) {
+            uint32_t r0, r1, r2, r3;
+            ldsm_x4(a + (uint32_t)ku * 32u, r0, r1, r2, r3);
+            const uint2 x0 = xw[ku * 8], x1 = xw[ku * 8 + 4];
+            mma_f16(d0, code2_f16x2<WK>(r0, false), code2_f16x2<WK>(r1, false), code2_f16x2<WK>(r0, true),
+                    code2_f16x2<WK>(r1, true), x0.x, x0.y);
+            mma_f16(d1, code2_f16x2<WK>(r2, false), code2_f16x2<WK>(r3, false), code2_f16x2<WK>(r2, true),
+                    code2_f16x2<WK>(r3, true), x1.x, x1.y);
+        }
+    }
+    s0 = d0[0] + d1[0];
+    s1 = d0[2] + d1[2];
+}
+
 // x (activation type) -> FP16 scaled by 2^-e, e chosen so max |x| = am lands in [2^14, 2^15);
 // each thread rewrites its own channel pairs (2t, 2t+1) + 512j.  Returns 2^e.  Out of line:
 // rarely taken, and the per-layer code of the kernel is instruction-cache bound.
@@ -602,6 +650,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int C = P.C, L = P.L, NH = P.NH, maxT = P.maxT, S = P.splits, G = P.G, NS = P.nsw;
+    const int LA = max(2, min(NS, P.lookahead));
     PeerSet peers;  // tensor parallel only (constant indices into the parameters)
     const PeerSet* pgp = nullptr;
     if constexpr (TPG) {
@@ -641,7 +690,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
     // paths read them from shared memory (no divisions or parameter loads there)
     PhaseRows* geo = reinterpret_cast<PhaseRows*>(sm + lay.geo);
     unsigned long long** obase = reinterpret_cast<unsigned long long**>(sm + lay.geo + 5 * sizeof(PhaseRows));
-    if constexpr (MMA && w8)  // the LayerNorm exponents, read once: global memory is far on the per-phase path
+    if constexpr (w8)  // the LayerNorm exponents, read once: global memory is far on the per-phase path
         for (int i = tid; i <= 2 * L; i += kThreads) reinterpret_cast<int*>(sm + lay.lnx)[i] = P.ln_exp[i];
     if (tid < 5) {
         geo[tid] = phase_rows<MMA>(P, tid, b);
@@ -675,14 +724,20 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                 else if (ph == kPhFcproj) bias = reinterpret_cast<const unsigned char*>(P.fcprojb);
                 if (bias) bias += (size_t)l * pr.M * kXB;
                 const float* scl = w8 ? P.S[widx] + (ph == kPhLm ? (size_t)P.v0 : (size_t)l * pr.M) : nullptr;
+                // look-ahead: the whole ring for the LM head, P.lookahead stages in the layers
+                const int ahead = ph == kPhLm ? NS : LA;
                 for (int r0 = pr.c0; r0 < pr.c1; r0 += pr.rs) {
                     const int nr = min(pr.rs, pr.c1 - r0);
                     for (int kq = 0; kq < pr.kparts; kq++) {
-                        if (issued >= NS) {  // wait until all consumer warps released this stage
-                            const uint32_t par = (uint32_t)(((issued / NS) - 1) & 1);
+                        if (issued >= ahead) {
+                            // wait until stage issued - ahead was released (which frees this slot
+                            // too: a slot's uses are released in order); ahead <= NS, so that
+                            // phase of its barrier is the latest with this parity
+                            const int j = issued - ahead;
+                            const uint32_t par = (uint32_t)((j / NS) & 1);
                             bool ok = false;
                             for (uint32_t i = 0; i < kMbarSpinLimit; ++i) {
-                                if (mbar_try_wait(&empty[st], par)) { ok = true; break; }
+                                if (mbar_try_wait(&empty[j % NS], par)) { ok = true; break; }
                                 if (*stop) break;
                             }
                             if (!ok) goto producer_drain;
@@ -708,7 +763,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                         // tokens of a call while the layers stream through (-1.8 % BF16, -4.3 % INT8
                         // per token; evict_last alone -0.3 %)
                         const uint64_t pol = ph == kPhLm ? pol_lm : pol_layer;
-                        if (rstride == part_bytes && pr.kparts == 1) {  // contiguous rows: one copy
+                        if (!MMA && WK != WK_F32 && ph == kPhLm) {  // row pairs for the LM head's tensor cores
+                            for (int i = 0; 2 * i < nr; i++)
+                                bulk_g2s_hint(sd + (size_t)i * (2 * part_bytes + 16), wl + (size_t)(r0 + 2 * i) * row_bytes,
+                                              (uint32_t)(min(2, nr - 2 * i) * part_bytes), &full[st], pol);
+                        } else if (rstride == part_bytes && pr.kparts == 1) {  // contiguous rows: one copy
                             bulk_g2s_hint(sd, wl + (size_t)r0 * row_bytes, (uint32_t)(nr * part_bytes), &full[st], pol);
                         } else {
                             for (int i = 0; i < nr; i++)
@@ -825,7 +884,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                 // ---------- x of this phase ----------
                 if (ph == kPhQkv || ph == kPhFc || lm) {
                     int ln_e = 0;
-                    if constexpr (MMA && w8)
+                    if constexpr (w8)
                         ln_e = reinterpret_cast<const int*>(sm + lay.lnx)[lm ? 2 * L : 2 * l + (ph == kPhFc ? 1 : 0)];
                     // residual update (fcproj of the previous layer, or proj), then LayerNorm;
                     // gamma and beta are loaded (narrow: into registers; wide: bulk-copied into
@@ -936,7 +995,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                         ln_par ^= 1u;
                         ln_pending = false;
                     }
-                    if constexpr (MMA && w8) {
+                    if constexpr (w8) {  // tensor-core stages: every phase (wide), the LM head (narrow)
                         x_down = __int_as_float((127 - ln_e) << 23);
                         x_up = __int_as_float((127 + ln_e) << 23);
                     }
@@ -948,7 +1007,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                             const float bb = WIDE ? to_f<XT>(lnp[C + c]) : lb[j];
                             const XT xvv = from_f<XT>((rstd * (res[c] - mean)) * g + bb);
                             xv[c] = xvv;
-                            if constexpr (MMA && w8) reinterpret_cast<__half*>(xh)[c] = __float2half_rn(to_f<XT>(xvv) * x_down);
+                            if constexpr (w8)
+                                if (MMA || lm) reinterpret_cast<__half*>(xh)[c] = __float2half_rn(to_f<XT>(xvv) * x_down);
                         }
                     }
                 } else {
@@ -1010,15 +1070,63 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                             ll_store(out + row, round_to<XT>(ph == kPhFc ? gelu_tanh(v) : v), tag);
                         }
                     };
-                    if (!MMA && lm) {
-                        // the LM head on CUDA cores, two stages per round: warp w takes rows w and
-                        // w + 8 of both (four sums sharing every x load); one K-part per row
+                    if (!MMA && WK != WK_F32 && lm) {
+                        // the LM head on the tensor cores, one warp per stage: stage k of this CTA
+                        // goes to warp k mod nw, which multiplies its 16 rows by x over all of K and
+                        // emits them, then releases the stage with the 8 arrivals its barrier counts.
+                        // nw divides the ring depth, so every ring slot is used by one warp only and
+                        // a warp never waits for a slot's phase more than one ahead of the last it
+                        // consumed there (a parity wait cannot tell phases two apart)
+                        int nw = kCW;
+                        while (NS % nw) nw--;
+                        const int lmrs = 2 * part_bytes + 16;
+                        const uint32_t a_lane =
+                            (uint32_t)((lane & 7) * lmrs + ((lane >> 3) & 1) * part_bytes + (lane >> 4) * 16);
+                        int k = 0;
+                        for (int r0 = pr.c0; r0 < pr.c1; r0 += pr.rs, ++k) {
+                            if (k % nw == warp) {
+                                const int nr = min(pr.rs, pr.c1 - r0);
+#ifdef GPT2B_PERSIST_TRACE
+                                if (lane == 0) { PTRACE_STAGE(1, consumed_n); PTRACE_STAGE(4, consumed_n); }
+#endif
+                                if (!mbar_wait(&full[cst], cpar)) bad = true;
+#ifdef GPT2B_PERSIST_TRACE
+                                if (lane == 0) PTRACE_STAGE(2, consumed_n);
+#endif
+                                const unsigned char* sd = ring + (size_t)cst * lay.stage_bytes;
+                                float s0, s1;
+                                lm_stage_mma<WK>(smem_addr(sd) + a_lane, w8 ? xh : xs, C, lane, s0, s1);
+                                if ((lane & 3) == 0) {
+                                    const int g = lane >> 2;
+                                    if (2 * g < nr) emit(sd, r0, 2 * g, w8 ? s0 * x_up : s0);
+                                    if (2 * g + 1 < nr) emit(sd, r0, 2 * g + 1, w8 ? s1 * x_up : s1);
+                                }
+                                __syncwarp();
+                                if (lane == 0) mbar_arrive_cnt(&empty[cst], kCW);
+#ifdef GPT2B_PERSIST_TRACE
+                                if (lane == 0) PTRACE_STAGE(3, consumed_n);
+#endif
+                            }
+                            if (++cst == NS) { cst = 0; cpar ^= 1u; }
+#ifdef GPT2B_PERSIST_TRACE
+                            consumed_n++;
+#endif
+                        }
+                    } else if (!MMA && lm) {
+                        // the LM head on CUDA cores (FP32 weights), two stages per round: warp w takes
+                        // rows w and w + 8 of both (four sums sharing every x load); one K-part per row
                         for (int r0 = pr.c0; r0 < pr.c1; r0 += 2 * pr.rs) {
                             const int na = min(pr.rs, pr.c1 - r0), nb = min(pr.rs, pr.c1 - r0 - pr.rs);
                             const int cb = cst + 1 == NS ? 0 : cst + 1;
                             const uint32_t pb = cst + 1 == NS ? cpar ^ 1u : cpar;
+#ifdef GPT2B_PERSIST_TRACE
+                            if (tid == 0) { PTRACE_STAGE(1, consumed_n); PTRACE_STAGE(4, consumed_n); }
+#endif
                             if (!mbar_wait(&full[cst], cpar)) bad = true;
                             if (nb > 0 && !mbar_wait(&full[cb], pb)) bad = true;
+#ifdef GPT2B_PERSIST_TRACE
+                            if (tid == 0) PTRACE_STAGE(2, consumed_n);
+#endif
                             const unsigned char* sa = ring + (size_t)cst * lay.stage_bytes;
                             const unsigned char* sb = ring + (size_t)cb * lay.stage_bytes;
                             const bool a1v = warp + kCW < na, b0v = warp < nb, b1v = warp + kCW < nb;
@@ -1060,6 +1168,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                             if (++cst == NS) { cst = 0; cpar ^= 1u; }
                             if (nb > 0 && ++cst == NS) { cst = 0; cpar ^= 1u; }
 #ifdef GPT2B_PERSIST_TRACE
+                            if (tid == 0) PTRACE_STAGE(3, consumed_n);
                             consumed_n += nb > 0 ? 2 : 1;
 #endif
                         }
@@ -1498,7 +1607,7 @@ cudaError_t launch_persist_t(const PersistParams& P, cudaStream_t st, int* smem_
 }
 
 cudaError_t persist_dispatch(int wk, int kv, const PersistParams& P, cudaStream_t st, int* smem_out) {
-    const int mode = P.tp_size > 1 ? 2 : ((P.C <= kNarrowC && P.kv_rows <= kNarrowKvRows) ? 0 : 1);
+    const int mode = P.tp_size > 1 ? 2 : (persist_narrow(P.C, P.kv_rows, P.tp_size) ? 0 : 1);
 #define GPT2B_PK(W_, K_) \
     if (wk == W_ && kv == K_)                                                   \
         return mode == 0 ? launch_persist_t<W_, K_, 0>(P, st, smem_out)       \
@@ -1583,6 +1692,7 @@ cudaError_t persist_ln_exponents(int* out, const void* ln1w, const void* ln1b, c
 
 int persist_max_splits() { return kMaxSplits; }
 int persist_max_stages() { return kMaxNs; }
+bool persist_narrow(int C, int kv_rows, int tp) { return tp <= 1 && C <= kNarrowC && kv_rows <= kNarrowKvRows; }
 
 int persist_stage_bytes(int wk, int C) { return kStageUnits * (C * wkind_bytes(wk) + 16) + kTail; }
 
