@@ -729,11 +729,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                 for (int r0 = pr.c0; r0 < pr.c1; r0 += pr.rs) {
                     const int nr = min(pr.rs, pr.c1 - r0);
                     for (int kq = 0; kq < pr.kparts; kq++) {
-                        if (issued >= ahead) {
-                            // wait until stage issued - ahead was released (which frees this slot
-                            // too: a slot's uses are released in order); ahead <= NS, so that
-                            // phase of its barrier is the latest with this parity
-                            const int j = issued - ahead;
+                        // wait until (a) the slot's previous use, stage issued - NS, and (b) the
+                        // look-ahead bound, stage issued - ahead, were released.  (a) is needed
+                        // on its own: the LM head's warps release their stages out of order, so
+                        // a later stage's release does not free an earlier stage's slot.  Every
+                        // earlier issue waited for its own (a), so neither barrier can be two
+                        // phases behind the parity waited for
+                        for (int q = 0; q < 2; q++) {
+                            const int j = issued - (q == 0 ? NS : ahead);
+                            if (j < 0 || (q == 1 && ahead == NS)) continue;
                             const uint32_t par = (uint32_t)((j / NS) & 1);
                             bool ok = false;
                             for (uint32_t i = 0; i < kMbarSpinLimit; ++i) {

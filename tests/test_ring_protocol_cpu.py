@@ -10,7 +10,13 @@ with nw the largest divisor of NS not above 8, so every slot is used by one
 warp only.  This model runs random completion orders and interleavings for
 every ring depth the engine can choose and checks that no wait is satisfied
 by the wrong phase -- and that the mapping k mod 8 does break for a ring of 4
-(the model catches it)."""
+(the model catches it).
+
+The producer runs at most LA stages ahead in the layer phases (LA <= NS) and NS
+in the LM head.  Before it fills slot g mod NS it must see both stage g - LA and
+stage g - NS released: after the LM head, whose warps release out of order, the
+look-ahead bound alone would let it overwrite a slot that a slower warp still
+reads (the model catches that too)."""
 from __future__ import annotations
 
 import random
@@ -27,10 +33,16 @@ def lm_warps(ns: int) -> int:
     return nw
 
 
-def simulate(ns: int, n_pre: int, n_lm: int, mapping, seed: int) -> str:
-    """Return "ok", "alias" (a wait passed on the wrong phase) or "deadlock"."""
+def simulate(ns: int, n_pre: int, n_lm: int, mapping, seed: int, la: int | None = None, n_post: int = 0,
+             slot_wait: bool = True) -> str:
+    """Return "ok", "alias" (a wait passed on the wrong phase), "overwrite" (a slot
+    refilled before its previous stage was released) or "deadlock".  Stages
+    [0, n_pre) and [n_pre + n_lm, total) are layer stages (all warps, look-ahead
+    la); the n_lm in between are LM stages (one warp each, look-ahead ns)."""
     rng = random.Random(seed)
-    total = n_pre + n_lm
+    la = ns if la is None else la
+    total = n_pre + n_lm + n_post
+    rel = set()  # released stages
     completed = [0] * ns  # full-barrier phases completed per slot
     released = [0] * ns   # empty-barrier phases completed per slot
     landed = set()        # stages whose copy landed
@@ -38,8 +50,11 @@ def simulate(ns: int, n_pre: int, n_lm: int, mapping, seed: int) -> str:
     in_flight = []        # issued, not landed
     # consumer state: per warp, its stages in order and the index of the next one
     stages_of = {w: [] for w in range(KCW)}
+    def is_lm(g):
+        return n_pre <= g < n_pre + n_lm
+
     for g in range(total):
-        if g < n_pre:
+        if not is_lm(g):
             for w in range(KCW):
                 stages_of[w].append(g)
         else:
@@ -55,9 +70,15 @@ def simulate(ns: int, n_pre: int, n_lm: int, mapping, seed: int) -> str:
         if steps > 200000:
             return "deadlock"
         moves = []
-        # producer: issue the next stage when stage issued - ns was released
-        if issued < total and (issued < ns or released[issued % ns] >= issued // ns):
-            moves.append(("issue", None))
+        # producer: issue the next stage when the look-ahead bound (and the slot's own
+        # previous use, if slot_wait) was released
+        if issued < total:
+            ahead = ns if is_lm(issued) else la
+            ok = issued < ahead or (issued - ahead) in rel
+            if slot_wait:
+                ok = ok and (issued < ns or (issued - ns) in rel)
+            if ok:
+                moves.append(("issue", None))
         if in_flight:
             moves.append(("land", None))
         for w in range(KCW):
@@ -65,6 +86,8 @@ def simulate(ns: int, n_pre: int, n_lm: int, mapping, seed: int) -> str:
                 g = stages_of[w][pos[w]]
                 if g >= n_pre and not done_pre_all:
                     continue  # the LM phase starts after a CTA barrier
+                if g >= n_pre + n_lm and not all(x in rel for x in range(n_pre, n_pre + n_lm)):
+                    continue  # and ends with one
                 slot, use = g % ns, g // ns
                 if (completed[slot] & 1) != (use & 1):  # try_wait.parity(use & 1) passes
                     moves.append(("consume", w))
@@ -74,6 +97,8 @@ def simulate(ns: int, n_pre: int, n_lm: int, mapping, seed: int) -> str:
             return "deadlock"
         kind, w = rng.choice(moves)
         if kind == "issue":
+            if issued >= ns and (issued - ns) not in rel:
+                return "overwrite"
             in_flight.append(issued)
             issued += 1
         elif kind == "land":
@@ -89,12 +114,14 @@ def simulate(ns: int, n_pre: int, n_lm: int, mapping, seed: int) -> str:
             if completed[slot] != use + 1:
                 return "alias"
             pos[w] += 1
-            if g < n_pre:
+            if not is_lm(g):
                 arrivals.setdefault(g, set()).add(w)
                 if len(arrivals[g]) == KCW:
                     released[slot] += 1
+                    rel.add(g)
             else:
                 released[slot] += 1  # one warp arrives with the count of 8
+                rel.add(g)
             if not done_pre_all and all(pos[x] >= sum(1 for s in stages_of[x] if s < n_pre) for x in range(KCW)):
                 done_pre_all = True
 
@@ -110,3 +137,19 @@ def test_lm_stage_per_warp_mapping_never_aliases(ns):
 def test_model_catches_the_eight_warp_mapping_on_a_ring_of_four():
     results = {simulate(4, n_pre=9, n_lm=22, mapping=lambda k, n: k % KCW, seed=s) for s in range(50)}
     assert "alias" in results
+
+
+@pytest.mark.parametrize("ns,la", [(7, 4), (14, 8), (8, 8), (6, 4), (24, 4)])
+def test_producer_waits_for_the_slot_and_the_look_ahead(ns, la):
+    nw = lm_warps(ns)
+    for seed in range(30):
+        r = simulate(ns, n_pre=2 * ns + 3, n_lm=22, mapping=lambda k, n: k % nw, seed=seed, la=la,
+                     n_post=2 * ns)
+        assert r == "ok", (ns, la, seed, r)
+
+
+def test_model_catches_a_producer_that_only_waits_for_the_look_ahead():
+    nw = lm_warps(7)
+    results = {simulate(7, n_pre=17, n_lm=22, mapping=lambda k, n: k % nw, seed=s, la=4, n_post=14,
+                        slot_wait=False) for s in range(200)}
+    assert "overwrite" in results
