@@ -633,6 +633,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
     float* misc = reinterpret_cast<float*>(sm + lay.misc);
     int* misc_i = reinterpret_cast<int*>(misc);
     volatile int* stop = misc_i + (kMiscFloats - 1);  // consumers left early: the producer stops
+    volatile int* lm_done = misc_i + (kMiscFloats - 2);  // steps whose LM head all consumers finished
     uint64_t* full = reinterpret_cast<uint64_t*>(sm + lay.bars);
     uint64_t* empty = full + kMaxNs;
     uint64_t* kv_bar = empty + kMaxNs;
@@ -684,6 +685,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
         mbar_init(kv_bar, 1);
         mbar_init(ln_bar, 1);
         *stop = 0;
+        *lm_done = 0;
         mbar_fence_init();
     }
     // the row geometry of every phase and the exchange bases, computed once: the per-phase
@@ -707,6 +709,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
         if (lane != 0) return;
         const uint64_t pol_lm = l2_evict_last_policy(), pol_layer = l2_evict_first_policy();
         int issued = 0, st = 0;
+        int skip_lo = 0, skip_hi = 0;  // the latest block of stages the LM head's warps issue
+        int lm_gate = -1;              // step of that block: wait for its LM head before the next issue
         for (int step = 0; step < P.n_steps; step++) {
             for (int u = 0; u <= 4 * L; u++) {
                 const int l = (u == 4 * L) ? 0 : (u >> 2);
@@ -726,9 +730,34 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                 const float* scl = w8 ? P.S[widx] + (ph == kPhLm ? (size_t)P.v0 : (size_t)l * pr.M) : nullptr;
                 // look-ahead: the whole ring for the LM head, P.lookahead stages in the layers
                 const int ahead = ph == kPhLm ? NS : LA;
+                // the narrow tensor-core LM head issues its own stages from NS on: the producer
+                // only counts them, and before its next issue waits until the consumers have
+                // finished the whole LM head (the warps advance the slots' barriers by several
+                // phases meanwhile; after that point every LM phase has completed, so its
+                // parity waits see each barrier at most one phase behind again)
+                const bool lm_self = !MMA && WK != WK_F32 && ph == kPhLm;
                 for (int r0 = pr.c0; r0 < pr.c1; r0 += pr.rs) {
                     const int nr = min(pr.rs, pr.c1 - r0);
+                    const bool skip = lm_self && r0 - pr.c0 >= NS * pr.rs;
                     for (int kq = 0; kq < pr.kparts; kq++) {
+                        if (skip) {
+                            if (skip_hi != issued) skip_lo = issued;  // a new block of skipped stages
+                            skip_hi = ++issued;
+                            lm_gate = step;
+                            if (++st == NS) st = 0;
+                            continue;
+                        }
+                        if (lm_gate >= 0) {
+                            bool ok = false;
+                            for (uint32_t i = 0; i < kMbarSpinLimit; ++i) {
+                                if (*lm_done > lm_gate) { ok = true; break; }
+                                if (*stop) break;
+                                __nanosleep(64);
+                            }
+                            if (!ok) goto producer_drain;
+                            __threadfence_block();
+                            lm_gate = -1;
+                        }
                         // wait until (a) the slot's previous use, stage issued - NS, and (b) the
                         // look-ahead bound, stage issued - ahead, were released.  (a) is needed
                         // on its own: the LM head's warps release their stages out of order, so
@@ -789,9 +818,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
             }
         }
     producer_drain:
-        // leave with none of this warp's copies in flight
+        // leave with none of this warp's copies in flight: the stages before an LM head's own
+        // block landed once its consumers finished it; the LM head's warps wait for their own
+        if (lm_gate >= 0)
+            for (uint32_t i = 0; i < kMbarSpinLimit && *lm_done <= lm_gate && !*stop; ++i) __nanosleep(64);
         for (int k = issued > NS ? issued - NS : 0; k < issued; k++)
-            mbar_wait(&full[k % NS], (uint32_t)((k / NS) & 1));
+            if (k < skip_lo || k >= skip_hi) mbar_wait(&full[k % NS], (uint32_t)((k / NS) & 1));
         return;
     }
 
@@ -1081,9 +1113,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                         // nw divides the ring depth, so every ring slot is used by one warp only and
                         // a warp never waits for a slot's phase more than one ahead of the last it
                         // consumed there (a parity wait cannot tell phases two apart)
+                        // The producer issues the first NS stages; every later stage k is issued by
+                        // its own warp into the slot it has just read (stage k - NS, the same warp
+                        // and slot), so a slot is refilled as soon as its warp is done with it.
                         int nw = kCW;
                         while (NS % nw) nw--;
                         const int lmrs = 2 * part_bytes + 16;
+                        const int nst = (pr.c1 - pr.c0 + pr.rs - 1) / pr.rs;
+                        const unsigned char* wlm = P.W[0] + (size_t)P.v0 * part_bytes;
+                        const unsigned char* slm = w8 ? reinterpret_cast<const unsigned char*>(P.S[0] + P.v0) : nullptr;
+                        const uint64_t pol_lm = l2_evict_last_policy();
                         const uint32_t a_lane =
                             (uint32_t)((lane & 7) * lmrs + ((lane >> 3) & 1) * part_bytes + (lane >> 4) * 16);
                         int k = 0;
@@ -1104,6 +1143,25 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                                     const int g = lane >> 2;
                                     if (2 * g < nr) emit(sd, r0, 2 * g, w8 ? s0 * x_up : s0);
                                     if (2 * g + 1 < nr) emit(sd, r0, 2 * g + 1, w8 ? s1 * x_up : s1);
+                                }
+                                if (k + NS < nst) {  // refill: stage k + NS into this slot
+                                    const int rn = r0 + NS * pr.rs, nrn = min(pr.rs, pr.c1 - rn);
+                                    uint32_t sb = 0;
+                                    size_t sa = 0;
+                                    if (w8) {
+                                        sa = ((size_t)rn * 4) & ~(size_t)15;
+                                        sb = (uint32_t)((((size_t)(rn + nrn) * 4 + 15) & ~(size_t)15) - sa);
+                                    }
+                                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // our reads first
+                                    __syncwarp();
+                                    unsigned char* sdw = ring + (size_t)cst * lay.stage_bytes;
+                                    if (lane == 0) mbar_arrive_expect_tx(&full[cst], (uint32_t)(nrn * part_bytes) + sb);
+                                    __syncwarp();
+                                    if (2 * lane < nrn)
+                                        bulk_g2s_hint(sdw + (size_t)lane * lmrs, wlm + (size_t)(rn + 2 * lane) * part_bytes,
+                                                      (uint32_t)(min(2, nrn - 2 * lane) * part_bytes), &full[cst], pol_lm);
+                                    if (w8 && lane == 0)
+                                        bulk_g2s(sdw + kStageUnits * (unit_bytes + 16) + kTailSlot, slm + sa, sb, &full[cst]);
                                 }
                                 __syncwarp();
                                 if (lane == 0) mbar_arrive_cnt(&empty[cst], kCW);
@@ -1295,6 +1353,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const Pe
                     }
                 }
                 if (cta_any(bad)) goto consumer_abort;
+                if (lm && tid == 0) {  // every LM stage of this step was consumed and released
+                    __threadfence_block();
+                    *lm_done = step + 1;
+                }
                 PTRACE(u * 3 + 1);
 
                 // ---------- after QKV: attention (head ah, split as) ----------

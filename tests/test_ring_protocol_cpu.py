@@ -34,7 +34,7 @@ def lm_warps(ns: int) -> int:
 
 
 def simulate(ns: int, n_pre: int, n_lm: int, mapping, seed: int, la: int | None = None, n_post: int = 0,
-             slot_wait: bool = True) -> str:
+             slot_wait: bool = True, self_refill: bool = False) -> str:
     """Return "ok", "alias" (a wait passed on the wrong phase), "overwrite" (a slot
     refilled before its previous stage was released) or "deadlock".  Stages
     [0, n_pre) and [n_pre + n_lm, total) are layer stages (all warps, look-ahead
@@ -64,6 +64,7 @@ def simulate(ns: int, n_pre: int, n_lm: int, mapping, seed: int, la: int | None 
     pos = {w: 0 for w in range(KCW)}
     arrivals = {}  # stage -> warps that finished it (general phases need all 8)
     done_pre_all = False
+    gate = False  # the producer skipped LM stages and has not yet seen the LM head finish
     steps = 0
     while True:
         steps += 1
@@ -71,14 +72,28 @@ def simulate(ns: int, n_pre: int, n_lm: int, mapping, seed: int, la: int | None 
             return "deadlock"
         moves = []
         # producer: issue the next stage when the look-ahead bound (and the slot's own
-        # previous use, if slot_wait) was released
+        # previous use, if slot_wait) was released -- parity waits on the empty barriers.
+        # self_refill: LM stages from ns on are issued by the warp that read the slot
+        # before; the producer only counts them and, before its next issue, waits until
+        # every LM stage was released (a flag the consumers set after the LM head)
         if issued < total:
-            ahead = ns if is_lm(issued) else la
-            ok = issued < ahead or (issued - ahead) in rel
-            if slot_wait:
-                ok = ok and (issued < ns or (issued - ns) in rel)
-            if ok:
-                moves.append(("issue", None))
+            if self_refill and is_lm(issued) and issued - n_pre >= ns:
+                moves.append(("skip", None))
+            elif not (gate and not all(x in rel for x in range(n_pre, n_pre + n_lm))):
+                ahead = ns if is_lm(issued) else la
+                waits = [issued - ahead] if issued >= ahead else []
+                if slot_wait and issued >= ns:
+                    waits.append(issued - ns)
+                ok = True
+                for j in waits:
+                    slot, use = j % ns, j // ns
+                    if (released[slot] & 1) != (use & 1):  # try_wait.parity passes
+                        if released[slot] != use + 1:
+                            return "alias"
+                    else:
+                        ok = False
+                if ok:
+                    moves.append(("issue", None))
         if in_flight:
             moves.append(("land", None))
         for w in range(KCW):
@@ -96,11 +111,15 @@ def simulate(ns: int, n_pre: int, n_lm: int, mapping, seed: int, la: int | None 
                 return "ok"
             return "deadlock"
         kind, w = rng.choice(moves)
-        if kind == "issue":
+        if kind == "skip":
+            issued += 1
+            gate = True
+        elif kind == "issue":
             if issued >= ns and (issued - ns) not in rel:
                 return "overwrite"
             in_flight.append(issued)
             issued += 1
+            gate = False
         elif kind == "land":
             g = in_flight.pop(rng.randrange(len(in_flight)))  # copies may complete out of order
             landed.add(g)
@@ -120,6 +139,8 @@ def simulate(ns: int, n_pre: int, n_lm: int, mapping, seed: int, la: int | None 
                     released[slot] += 1
                     rel.add(g)
             else:
+                if self_refill and is_lm(g + ns):
+                    in_flight.append(g + ns)  # the warp refills its slot before releasing it
                 released[slot] += 1  # one warp arrives with the count of 8
                 rel.add(g)
             if not done_pre_all and all(pos[x] >= sum(1 for s in stages_of[x] if s < n_pre) for x in range(KCW)):
@@ -139,13 +160,54 @@ def test_model_catches_the_eight_warp_mapping_on_a_ring_of_four():
     assert "alias" in results
 
 
+@pytest.mark.parametrize("self_refill", [False, True])
 @pytest.mark.parametrize("ns,la", [(7, 4), (14, 8), (8, 8), (6, 4), (24, 4)])
-def test_producer_waits_for_the_slot_and_the_look_ahead(ns, la):
+def test_producer_waits_for_the_slot_and_the_look_ahead(ns, la, self_refill):
+    """Also with the LM head's warps refilling their own slots from stage NS on."""
     nw = lm_warps(ns)
     for seed in range(30):
         r = simulate(ns, n_pre=2 * ns + 3, n_lm=22, mapping=lambda k, n: k % nw, seed=seed, la=la,
-                     n_post=2 * ns)
+                     n_post=2 * ns, self_refill=self_refill)
         assert r == "ok", (ns, la, seed, r)
+
+
+def test_model_catches_a_producer_that_tracks_self_refilled_stages_by_parity():
+    """The first self-refill design: the producer waited on the empty barrier for each
+    self-refilled stage's predecessor; the warps can advance a slot two phases past it."""
+    nw = lm_warps(7)
+
+    def run(seed):
+        return simulate_parity_tracking_producer(7, 17, 22, nw, seed)
+    assert "alias" in {run(s) for s in range(300)}
+
+
+def simulate_parity_tracking_producer(ns, n_pre, n_lm, nw, seed):
+    """Self-refilling warps, and a producer that waits (by parity) for the release of
+    stage g - ns before counting each self-refilled stage g."""
+    rng = random.Random(seed)
+    released = [0] * ns
+    consumed = {w: 0 for w in range(nw)}  # LM stages consumed per warp
+    lm_stages = {w: [k for k in range(n_lm) if k % nw == w] for w in range(nw)}
+    g = ns  # next self-refilled LM stage the producer counts
+    for _ in range(10000):
+        moves = [w for w in range(nw) if consumed[w] < len(lm_stages[w])]
+        if g < n_lm:
+            moves.append(-1)
+        if not moves:
+            return "ok"
+        m = rng.choice(moves)
+        if m == -1:
+            j = n_pre + g - ns
+            slot, use = j % ns, j // ns
+            if (released[slot] & 1) != (use & 1):
+                if released[slot] != use + 1:
+                    return "alias"
+                g += 1
+        else:
+            k = lm_stages[m][consumed[m]]
+            released[(n_pre + k) % ns] += 1  # consumed, refilled, released
+            consumed[m] += 1
+    return "ok"
 
 
 def test_model_catches_a_producer_that_only_waits_for_the_look_ahead():
