@@ -38,6 +38,16 @@ def test_plan_rejects_bad_groups(gpt2b):
             tp.plan(weights.GPT2_XL, rank, size)
 
 
+def test_plan_rejects_more_ranks_than_heads(gpt2b):
+    """Every rank owns at least one head: 5 heads over 8 ranks is refused (the engine
+    returns GPT2B_ERR_UNSUPPORTED), 5 over 4 is planned 2/1/1/1."""
+    from cuda_gpt2_inference_b200 import tp
+    mini = dict(maxT=64, V=250, L=2, NH=5, C=320, Vp=256)
+    with pytest.raises(gpt2b.Gpt2bError):
+        tp.plan(mini, 0, 8)
+    assert [tp.plan(mini, r, 4)["heads"] for r in range(4)] == [2, 1, 1, 1]
+
+
 def _tensors(image: bytes, cfg: dict, w8: bool) -> dict:
     """The 16 tensors of an image as arrays (uint8 codes for 8-bit Linear groups,
     uint16 bf16 bits otherwise)."""

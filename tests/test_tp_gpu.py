@@ -2,7 +2,7 @@
 persistent kernel with peer stores between the ranks ("p2p") and the
 per-kernel path with NCCL collectives ("nccl").
 
-* A GPT-2-XL-shaped miniature (5 heads, uneven over the ranks) in BF16 and
+* A GPT-2-XL-shaped miniature (5 heads, uneven over 2 and 4 ranks) in BF16 and
   INT8 + 8-bit KV.
 * The real GPT-2-XL width (C = 1600, 25 heads: 13/12, 7/6/6/6 and 4/3x7 over
   the ranks, FC 6400) with 2 layers, INT8 weights and BF16 KV.
@@ -95,7 +95,7 @@ def xl_width(gpt2b, cuda):
 
 
 @pytest.mark.parametrize("path", ["p2p", "nccl"])
-@pytest.mark.parametrize("size", [2, 4, 8])
+@pytest.mark.parametrize("size", [2, 4])  # 5 heads: a group of 8 is refused (tests/test_tp_cpu.py)
 @pytest.mark.parametrize("wmode,kvmode", [("bf16", "floatx"), ("int8", "8bit")])
 def test_tp_group_matches_single_gpu(mini_xl, orc, gpt2b, wmode, kvmode, size, path):
     cfg, imgs = mini_xl
